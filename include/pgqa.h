@@ -1,0 +1,150 @@
+/*
+ * pgqa.h - C ABI of the B200 (sm_100a) paged grouped-query-attention decode library
+ * (libpgqa.so).
+ *
+ * The library computes, for every sequence b and query head h,
+ *
+ *     kv       = h / (num_heads / num_heads_k)
+ *     tokens   = the first seq_lens[b] tokens of the paged cache of sequence b,
+ *                token t living in page block_table[b, t / page_size] at slot t % page_size
+ *     out[b,h] = softmax(scale * q[b,h] . K[tokens, kv]^T) . V[tokens, kv]
+ *
+ * with bf16 inputs/outputs and fp32 accumulation.  Layouts (all contiguous):
+ *     q, out        [B, 1, Hq, D]                    bf16
+ *     k, v pools    [num_pages, page_size, Hkv, D]   bf16
+ *     seq_lens      [B]                              int32
+ *     block_table   [B, bt_stride]                   int32
+ *
+ * Only the first ceil(seq_lens[b] / page_size) entries of a block-table row are
+ * ever read; padding slots may hold any value.
+ *
+ * All entry points are asynchronous with respect to the host (no device
+ * synchronisation inside), except the ones documented as "synchronous".
+ */
+#ifndef PGQA_H_
+#define PGQA_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes returned by the int-returning entry points. */
+enum pgqa_status {
+    PGQA_OK = 0,
+    PGQA_ERR_NULL_POINTER = 1,      /* a required pointer is NULL                       */
+    PGQA_ERR_BAD_SHAPE = 2,         /* B/Hq/Hkv/D/page_size/num_pages/stride invalid    */
+    PGQA_ERR_UNSUPPORTED = 3,       /* valid but not implemented (D != 128, Sq != 1 ...) */
+    PGQA_ERR_MISALIGNED = 4,        /* a pointer violates the alignment contract        */
+    PGQA_ERR_WORKSPACE = 5,         /* workspace missing / too small / allocation failed */
+    PGQA_ERR_CUDA = 6,              /* a CUDA runtime/driver call failed                */
+    PGQA_ERR_NO_DEVICE = 7,         /* no usable CUDA device (or not sm_100)            */
+    PGQA_ERR_DEVICE_TIMEOUT = 8,    /* a bounded device-side wait expired (device word) */
+    PGQA_ERR_DEVICE_BAD_PAGE = 9,   /* a block-table entry was outside [0, num_pages)   */
+    PGQA_ERR_DEVICE_BAD_SEQLEN = 10 /* a seq_len was < 0 or above the table capacity    */
+};
+
+/*
+ * Reference drop-in.  Replaces `extern "C" void run_kernel(...)` of the MetaX C500
+ * submission (submission_clean.cu:432-447; contract task.md:33-54), with the same
+ * symbol name, argument types, order and meaning:
+ *   block_table row width = num_blocks / batch_size, pool size = num_blocks pages,
+ *   scale = 1/sqrt(headdim), launches on the legacy default stream, returns void.
+ * Errors (which the reference ignores) are recorded and can be read back with
+ * pgqa_last_status().  The first call on a device allocates the library's
+ * per-device workspace (cudaMalloc), so the first call must not be inside a
+ * CUDA-graph capture.
+ */
+void run_kernel(const void* q, const void* k_cache_paged, const void* v_cache_paged,
+                void* output, const int32_t* cache_seqlens, const int32_t* block_table,
+                int64_t batch_size, int64_t seqlen_k, int64_t seqlen_q, int64_t num_heads,
+                int64_t num_heads_k, int64_t headdim, int64_t page_block_size,
+                int64_t num_blocks, int64_t causal);
+
+/*
+ * Extended entry point (no counterpart symbol in the reference; it generalises
+ * run_kernel, submission_clean.cu:432-504, for pools whose page count is not
+ * batch_size * table width and for an explicit scale/stream).
+ *   num_pages   : pages in each K/V pool (TMA bounds; entries >= num_pages are errors)
+ *   bt_stride   : block_table row stride in int32 elements
+ *   max_seqlen  : capacity bound in tokens (<= bt_stride * page_size); 0 = derive
+ *   scale       : softmax scale (e.g. 1/sqrt(D))
+ *   workspace   : device buffer of >= pgqa_workspace_size(...) bytes, zero-filled
+ *                 once before first use (pgqa_workspace_init); the kernel leaves it
+ *                 zeroed.  NULL = use the library's per-device workspace.
+ *   stream      : cudaStream_t (NULL = legacy default stream)
+ * Calls that share one workspace must be ordered on one stream.
+ */
+int pgqa_decode_v1(const void* q, const void* k_cache, const void* v_cache, void* out,
+                   const int32_t* seq_lens, const int32_t* block_table, int64_t batch_size,
+                   int64_t num_heads, int64_t num_heads_k, int64_t headdim,
+                   int64_t page_size, int64_t num_pages, int64_t bt_stride,
+                   int64_t max_seqlen, float scale, void* workspace, size_t workspace_bytes,
+                   void* stream);
+
+/* Bytes of workspace pgqa_decode_v1 needs for this shape on the current device
+ * (no counterpart in the reference, whose workspace is a hidden static buffer,
+ * submission_clean.cu:478-491).  Returns 0 on invalid shapes. */
+size_t pgqa_workspace_size(int64_t batch_size, int64_t num_heads, int64_t num_heads_k,
+                           int64_t headdim, int64_t page_size);
+
+/* Zero a caller-provided workspace on `stream` (asynchronous). */
+int pgqa_workspace_init(void* workspace, size_t workspace_bytes, void* stream);
+
+/* Status of the most recent run_kernel / pgqa_decode_v1 call on this host thread. */
+int pgqa_last_status(void);
+
+/* Human-readable text for a status code (static storage). */
+const char* pgqa_status_string(int status);
+
+/* Synchronous: waits for `stream`, reads and clears the device-side error word of
+ * `workspace` (NULL = the library workspace of the current device).  Returns
+ * PGQA_OK or one of the PGQA_ERR_DEVICE_* codes. */
+int pgqa_check_device_error(void* workspace, void* stream);
+
+/*
+ * Launch plan (host-only, no GPU needed).  Reproduces the decisions the launcher
+ * makes for a shape: replaces the reference's choose_num_splits
+ * (submission_clean.cu:375-430) and its page rounding (:453-461).
+ */
+typedef struct pgqa_plan {
+    int32_t grid_ctas;        /* persistent CTAs launched (one per SM)               */
+    int32_t warps_per_cta;    /* streaming warps per CTA                              */
+    int32_t stages;           /* TMA ring depth per warp (16-token stages)            */
+    int32_t min_chunks_per_warp; /* lower bound on work per active warp (chunks)      */
+    int32_t head_groups;      /* query-head groups of <= 8 per KV head               */
+    int32_t units_per_seq;    /* num_heads_k * head_groups                            */
+    int32_t smem_bytes;       /* dynamic shared memory per CTA                        */
+    int32_t status;           /* PGQA_OK or why the shape cannot run                  */
+    int64_t workspace_bytes;  /* pgqa_workspace_size for this shape                   */
+} pgqa_plan;
+
+/* Fill *plan for a shape on a device with `num_sms` SMs and `smem_per_block_optin`
+ * bytes of opt-in shared memory (pass 0, 0 to use B200 values: 148, 232448). */
+int pgqa_make_plan(int64_t batch_size, int64_t num_heads, int64_t num_heads_k,
+                   int64_t headdim, int64_t page_size, int32_t num_sms,
+                   int32_t smem_per_block_optin, pgqa_plan* plan);
+
+/*
+ * Host simulation of the device work partition for given seq_lens (host array).
+ * For each unit u = (b, kv, head_group) (b-major, B * units_per_seq entries) it
+ * writes the number of CTAs whose slice intersects the unit (ctas_per_unit) and
+ * the number of warp segments it is cut into (segments_per_unit), and returns the
+ * number of active CTAs.  Used by the CPU tests to check that the split is exact
+ * (every 16-token chunk is owned by exactly one warp).  Returns < 0 on error.
+ */
+int64_t pgqa_simulate_partition(const int32_t* seq_lens, int64_t batch_size,
+                                int64_t units_per_seq, int64_t bt_capacity_tokens,
+                                const pgqa_plan* plan, int32_t* ctas_per_unit,
+                                int32_t* segments_per_unit);
+
+/* Library build identifier (static storage). */
+const char* pgqa_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PGQA_H_ */

@@ -1,0 +1,1162 @@
+/*
+ * pgqa_decode.cu - paged grouped-query-attention decode for B200 (sm_100a).
+ *
+ * Replaces, behind the same `run_kernel` C symbol, the reference's
+ *   - split-KV partial kernel   paged_gqa_mma_kernel   (submission_clean.cu:66-300;
+ *     online-softmax form paged_gqa_decode_mma, optimized_c500_flash_attn.cu:463-664)
+ *   - split combine             combine_kernel         (submission_clean.cu:307-360;
+ *     LSE form combine_splits, optimized_c500_flash_attn.cu:666-728)
+ *   - split-count policy        choose_num_splits      (submission_clean.cu:375-430)
+ *   - host prologue / launcher  run_kernel             (submission_clean.cu:432-504)
+ *
+ * Design (one launch per call):
+ *   * Persistent grid, one CTA per SM, W streaming warps per CTA.  The total work,
+ *     measured in 16-token chunks of the *actual* sequence lengths, is cut into equal
+ *     contiguous slices per CTA and per warp (pgqa_partition.h).  The per-unit split
+ *     count therefore follows from B*Hkv, the lengths and the SM count; there are no
+ *     per-case constants and no empty splits.
+ *   * Each warp owns an S-stage ring of 8 KB stages in shared memory.  Lane 0 issues
+ *     four TMA tile loads per stage (K and V, two 64-dim halves each, 16 tokens of one
+ *     KV head, 128-byte swizzle) that complete on the stage's mbarrier.  Page ids come
+ *     from a 32-entry block-table window loaded by the whole warp; only the first
+ *     ceil(L_b / page_size) entries of a row are ever read.
+ *   * Math per 16-token stage, tokens in the MMA M dimension ("swap AB"), the GQA group
+ *     (<= 8 query heads) in N:  S^T = K.Q^T (8 x mma.m16n8k16 bf16), fp32 online softmax
+ *     in the log2 domain (scale*log2e folded into one multiply, ex2.approx), P^T moved
+ *     into the B-operand layout with movmatrix.trans, O^T += V^T.P^T (8 x mma).
+ *   * A unit (b, kv, head-group) that lies inside one warp's slice is normalised and
+ *     stored as bf16 directly.  Units cut by warp boundaries are merged in shared
+ *     memory at the end of the CTA; units cut by CTA boundaries write an fp32 record
+ *     (o, log2-sum-exp) to the workspace, and the last CTA to finish the unit (atomic
+ *     counter, reset by that CTA) merges the records -- the LSE combine, fused.
+ */
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <math.h>
+#include <mutex>
+
+#include "../../include/pgqa.h"
+#include "pgqa_partition.h"
+#include "pgqa_ptx.cuh"
+
+namespace pgqa {
+
+/* ------------------------------------------------------------------------------------ */
+/* Device side                                                                          */
+/* ------------------------------------------------------------------------------------ */
+
+constexpr int kStageBytes = 8192;          // K (2 x 2 KB halves) + V (2 x 2 KB halves)
+constexpr int kHalfBytes = 2048;           // 16 tokens x 64 dims x bf16
+constexpr int kStashRow = 132;             // padded fp32 row (bank-conflict free stores)
+constexpr uint64_t kWaitLimitNs = 1000000000ull;  // 1 s bound on any single wait
+
+enum DeviceErr : int32_t { kErrTimeout = 1, kErrBadPage = 2, kErrBadSeqlen = 4 };
+
+struct DecodeParams {
+    const __nv_bfloat16* q;
+    __nv_bfloat16* out;
+    const int32_t* seq_lens;
+    const int32_t* block_table;
+    float* rec_o;        // [2 * grid][8][128]
+    float* rec_lse;      // [2 * grid][8]
+    int32_t* counters;   // [B * U]
+    int32_t* err;        // device error word
+    int32_t B, Hq, Hkv, g, n_hg, U;
+    int32_t page_size, bt_stride, num_pages;
+    int64_t cap_tokens;  // bt_stride * page_size (clamp for seq_lens)
+    float scale_log2;    // scale * log2(e)
+    int32_t min_chunks;
+    int32_t debug_stuck;     // test hook: CTA 0 / warp 0 first stage expects 16 bytes too many
+    uint64_t wait_limit_ns;  // bound on every mbarrier wait
+};
+
+/* Per-warp record of a unit cut by a slice boundary (shared memory, after streaming). */
+struct __align__(16) Stash {
+    float o[8][kStashRow];  // normalised o[h][d]
+    float lse[8];           // log2-sum-exp per head
+    int32_t b, j, valid, pad;
+};
+
+struct Cursor {
+    int32_t b, j, c, n, L;  // sequence, unit-in-sequence, chunk-in-unit, chunks, length
+};
+
+__device__ __forceinline__ int32_t clamp_len(int32_t L, int64_t cap) {
+    if (L < 0) return 0;
+    if ((int64_t)L > cap) return (int32_t)cap;
+    return L;
+}
+
+/* Largest b with pre[b]*U <= x  (x < pre[B]*U). */
+__device__ __forceinline__ int32_t find_seq(const uint32_t* pre, int32_t B, int64_t U, int64_t x) {
+    int32_t lo = 0, hi = B;
+    while (hi - lo > 1) {
+        const int32_t mid = (lo + hi) >> 1;
+        if ((int64_t)pre[mid] * U <= x) lo = mid; else hi = mid;
+    }
+    return lo;
+}
+
+__device__ __forceinline__ Cursor locate(const DecodeParams& p, const uint32_t* pre, int64_t x) {
+    Cursor cu;
+    cu.b = find_seq(pre, p.B, p.U, x);
+    cu.n = (int32_t)(pre[cu.b + 1] - pre[cu.b]);
+    const int64_t r = x - (int64_t)pre[cu.b] * p.U;
+    cu.j = (int32_t)(r / cu.n);
+    cu.c = (int32_t)(r - (int64_t)cu.j * cu.n);
+    cu.L = clamp_len(__ldg(p.seq_lens + cu.b), p.cap_tokens);
+    return cu;
+}
+
+/* Step to the next chunk.  Must only be called when a next chunk exists. */
+__device__ __forceinline__ void advance(const DecodeParams& p, const uint32_t* pre, Cursor& cu) {
+    if (++cu.c < cu.n) return;
+    cu.c = 0;
+    if (++cu.j < p.U) return;
+    cu.j = 0;
+    do { ++cu.b; } while (pre[cu.b + 1] == pre[cu.b]);
+    cu.n = (int32_t)(pre[cu.b + 1] - pre[cu.b]);
+    cu.L = clamp_len(__ldg(p.seq_lens + cu.b), p.cap_tokens);
+}
+
+__device__ __forceinline__ int64_t unit_begin(const DecodeParams& p, const uint32_t* pre, int32_t b,
+                                              int32_t j) {
+    return (int64_t)pre[b] * p.U + (int64_t)j * (pre[b + 1] - pre[b]);
+}
+
+/* Merge `cnt` stashes (LSE merge) for head h, dims [d0, d0+4); result in acc / lse. */
+struct MergeAcc {
+    float m, den;
+    float a[4];
+    __device__ __forceinline__ void init() {
+        m = -INFINITY; den = 0.f; a[0] = a[1] = a[2] = a[3] = 0.f;
+    }
+    __device__ __forceinline__ void add(float lse, float4 o) {
+        if (lse > m) {
+            const float s = ptx::ex2(m - lse);  // 0 when m == -inf
+            den *= s; a[0] *= s; a[1] *= s; a[2] *= s; a[3] *= s;
+            m = lse;
+        }
+        const float w = ptx::ex2(lse - m);
+        den += w;
+        a[0] = fmaf(w, o.x, a[0]); a[1] = fmaf(w, o.y, a[1]);
+        a[2] = fmaf(w, o.z, a[2]); a[3] = fmaf(w, o.w, a[3]);
+    }
+};
+
+__device__ __forceinline__ void store_bf16x4(__nv_bfloat16* dst, float x, float y, float z, float w) {
+    uint2 v;
+    v.x = ptx::pack_bf16x2(x, y);
+    v.y = ptx::pack_bf16x2(z, w);
+    *reinterpret_cast<uint2*>(dst) = v;
+}
+
+template <int W, int S>
+__global__ void __launch_bounds__(W * 32, 1)
+pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
+                   const __grid_constant__ CUtensorMap vmap, const DecodeParams p) {
+    constexpr int NT = W * 32;
+    extern __shared__ uint8_t smem_raw[];
+    // 128-byte TMA swizzle needs 1024-byte aligned stages (shared-window offset).
+    uint8_t* smem = smem_raw + ((1024u - (ptx::smem_u32(smem_raw) & 1023u)) & 1023u);
+    uint8_t* ring = smem;                                                  // W*S*8 KB
+    uint64_t* bars = reinterpret_cast<uint64_t*>(ring + W * S * kStageBytes);  // W*S
+    int32_t* misc = reinterpret_cast<int32_t*>(bars + W * S);               // 32 ints
+    uint32_t* pre = reinterpret_cast<uint32_t*>(misc + 32);                 // B+1
+    Stash* stash = reinterpret_cast<Stash*>(ring);                          // reuses the ring
+
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5;
+    const int lane = tid & 31;
+    const int gid = lane >> 2;  // MMA group id (row within an 8-row block)
+    const int tig = lane & 3;   // thread in group
+
+    if (tid == 0) {
+        ptx::prefetch_tensormap(&kmap);
+        ptx::prefetch_tensormap(&vmap);
+        for (int i = 0; i < W * S; ++i) ptx::mbar_init(ptx::smem_u32(bars + i), 1);
+        ptx::fence_mbar_init();
+        misc[8] = -1;  // global-merge flags for record slot 0 / 1 (unit b)
+        misc[9] = -1;  // (unit j)
+        misc[10] = -1;
+        misc[11] = -1;
+    }
+
+    /* ---- chunk prefix over sequences (every CTA computes it; B is small) ---- */
+    {
+        const int per = (p.B + NT - 1) / NT;
+        const int b0 = min(p.B, tid * per);
+        const int b1 = min(p.B, b0 + per);
+        uint32_t local = 0;
+        int32_t bad = 0;
+        for (int b = b0; b < b1; ++b) {
+            const int32_t L = __ldg(p.seq_lens + b);
+            if (L < 0 || (int64_t)L > p.cap_tokens) bad = 1;
+            local += (uint32_t)seq_chunks(L, p.cap_tokens);
+        }
+        if (bad && blockIdx.x == 0) atomicOr(p.err, kErrBadSeqlen);
+        uint32_t incl = local;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t v = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += v;
+        }
+        if (lane == 31) misc[warp] = (int32_t)incl;
+        __syncthreads();
+        uint32_t base = 0;
+        for (int w2 = 0; w2 < warp; ++w2) base += (uint32_t)misc[w2];
+        uint32_t run = base + incl - local;
+        for (int b = b0; b < b1; ++b) {
+            pre[b] = run;
+            run += (uint32_t)seq_chunks(__ldg(p.seq_lens + b), p.cap_tokens);
+        }
+        if (tid == NT - 1) pre[p.B] = base + incl;
+        __syncthreads();
+    }
+
+    /* Zero-length sequences produce zeros (softmax over an empty set), written by CTA 0. */
+    if (blockIdx.x == 0) {
+        for (int b = tid; b < p.B; b += NT) {
+            if (pre[b + 1] == pre[b]) {
+                uint4* o4 = reinterpret_cast<uint4*>(p.out + (int64_t)b * p.Hq * kHeadDim);
+                for (int i = 0; i < p.Hq * kHeadDim / 8; ++i) o4[i] = make_uint4(0, 0, 0, 0);
+            }
+        }
+    }
+
+    const int64_t U = p.U;
+    const int64_t T = (int64_t)pre[p.B] * U;
+    if (T == 0) return;
+    const int64_t nct = active_ctas(T, gridDim.x, W, p.min_chunks);
+    if ((int64_t)blockIdx.x >= nct) return;
+    const int64_t cs = slice_begin(blockIdx.x, nct, T);
+    const int64_t ce = slice_begin(blockIdx.x + 1, nct, T);
+    const int64_t clen = ce - cs;
+    const int wa = (int)active_warps(clen, W);
+
+    const uint32_t ring_base = ptx::smem_u32(ring);
+    const uint32_t bar_base = ptx::smem_u32(bars);
+    const uint64_t pol = ptx::policy_evict_first();
+
+    /* Per-warp streaming state kept until the CTA-level merge. */
+    bool have_first = false, have_last = false;
+    Cursor first_u{}, last_u{};
+    float fo[8][4];
+    float flse[2] = {0.f, 0.f};
+    float o[8][4];
+    float m2[2], l2[2];
+    bool aborted = false;
+
+    if (warp < wa) {
+        const int64_t ws = cs + slice_begin(warp, wa, clen);
+        const int64_t we = cs + slice_begin(warp + 1, wa, clen);
+        const int64_t ntot = we - ws;
+
+        Cursor ic = locate(p, pre, ws);
+        Cursor cc = ic;
+
+        int32_t win_b = -1, win_p0 = 0, win_pid = 0;
+        int64_t issued = 0;
+        const int P = p.page_size;
+
+        auto issue_next = [&]() {
+            const int32_t tok = ic.c * kChunkTokens;
+            const int32_t page = tok / P;
+            const int32_t off = tok - page * P;
+            if (ic.b != win_b || page < win_p0 || page >= win_p0 + 32) {
+                win_b = ic.b;
+                win_p0 = page;
+                const int32_t npg = (ic.L + P - 1) / P;
+                const int32_t pg = page + lane;
+                win_pid = (pg < npg) ? __ldg(p.block_table + (int64_t)ic.b * p.bt_stride + pg) : 0;
+            }
+            int32_t pid = __shfl_sync(0xffffffffu, win_pid, page - win_p0);
+            if (lane == 0) {
+                if ((uint32_t)pid >= (uint32_t)p.num_pages) {
+                    atomicOr(p.err, kErrBadPage);
+                    pid = 0;
+                }
+                const int stage = (int)(issued % S);
+                const uint32_t bar = bar_base + (uint32_t)(warp * S + stage) * 8u;
+                const uint32_t dst = ring_base + (uint32_t)(warp * S + stage) * kStageBytes;
+                const int32_t kvh = ic.j / p.n_hg;
+                const int32_t z = pid * P + off;
+                const uint32_t extra =
+                    (p.debug_stuck && blockIdx.x == 0 && warp == 0 && issued == 0) ? 16u : 0u;
+                ptx::fence_proxy_async_smem();
+                ptx::mbar_arrive_expect_tx(bar, kStageBytes + extra);
+                ptx::tma_load_3d(dst, &kmap, bar, 0, kvh, z, pol);
+                ptx::tma_load_3d(dst + kHalfBytes, &kmap, bar, 64, kvh, z, pol);
+                ptx::tma_load_3d(dst + 2 * kHalfBytes, &vmap, bar, 0, kvh, z, pol);
+                ptx::tma_load_3d(dst + 3 * kHalfBytes, &vmap, bar, 64, kvh, z, pol);
+            }
+            ++issued;
+            if (issued < ntot) advance(p, pre, ic);
+        };
+
+        const int64_t prologue = ntot < S ? ntot : S;
+        for (int64_t k = 0; k < prologue; ++k) issue_next();
+
+        uint32_t qf[16];
+        int nh_valid = 0;
+        auto load_q = [&](const Cursor& cu) {
+            const int32_t kvh = cu.j / p.n_hg;
+            const int32_t hg = cu.j - kvh * p.n_hg;
+            nh_valid = min(kHeadsPerGroup, p.g - hg * kHeadsPerGroup);
+            if (gid < nh_valid) {
+                const uint32_t* qp = reinterpret_cast<const uint32_t*>(
+                    p.q + ((int64_t)cu.b * p.Hq + kvh * p.g + hg * kHeadsPerGroup + gid) * kHeadDim);
+#pragma unroll
+                for (int ks = 0; ks < 8; ++ks) {
+                    qf[2 * ks] = __ldg(qp + 8 * ks + tig);
+                    qf[2 * ks + 1] = __ldg(qp + 8 * ks + 4 + tig);
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) qf[i] = 0u;
+            }
+        };
+        auto reset_state = [&]() {
+            m2[0] = m2[1] = -INFINITY;
+            l2[0] = l2[1] = 0.f;
+#pragma unroll
+            for (int mt = 0; mt < 8; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+        };
+
+        load_q(cc);
+        reset_state();
+        bool unit_start_seen = (cc.c == 0);
+        int units_done = 0;
+
+        /* Per-lane ldmatrix offsets inside a stage (128-byte swizzle: 16-byte chunk
+         * index XOR (row & 7)). */
+        const int mj = lane >> 3;  // which 8x8 matrix this lane addresses
+        const int mr = lane & 7;   // row within that matrix
+        const int tK = mr + 8 * (mj & 1);
+        const int tV = mr + 8 * (mj >> 1);
+
+        for (int64_t i = 0; i < ntot; ++i) {
+            const int stage = (int)(i % S);
+            const uint32_t bar = bar_base + (uint32_t)(warp * S + stage) * 8u;
+            if (!ptx::wait_parity_bounded(bar, (uint32_t)((i / S) & 1), p.wait_limit_ns)) {
+                if (lane == 0) atomicOr(p.err, kErrTimeout);
+                aborted = true;
+                // Drain: wait (bounded) for every copy still in flight into this ring.
+                for (int64_t k = i; k < issued; ++k) {
+                    const uint32_t b2 = bar_base + (uint32_t)(warp * S + (int)(k % S)) * 8u;
+                    ptx::wait_parity_bounded(b2, (uint32_t)((k / S) & 1), p.wait_limit_ns);
+                }
+                break;
+            }
+            const uint32_t sK = ring_base + (uint32_t)(warp * S + stage) * kStageBytes;
+            const uint32_t sV = sK + 2 * kHalfBytes;
+
+            const bool last_of_unit = (cc.c == cc.n - 1);
+            const int nvalid = last_of_unit ? (cc.L - cc.c * kChunkTokens) : kChunkTokens;
+            if (nvalid < kChunkTokens) {
+                /* Tokens past the sequence end inside the last page: zero their V rows so
+                 * that p = 0 never meets a non-finite V value (0 * NaN). */
+                uint8_t* vrow = ring + (size_t)(warp * S + stage) * kStageBytes + 2 * kHalfBytes;
+                const int units = (kChunkTokens - nvalid) * 16;  // 16-byte pieces, both halves
+                for (int u = lane; u < units; u += 32) {
+                    const int t = nvalid + (u >> 4);
+                    const int half = (u >> 3) & 1;
+                    const int c16 = u & 7;
+                    *reinterpret_cast<uint4*>(vrow + half * kHalfBytes + t * 128 + c16 * 16) =
+                        make_uint4(0, 0, 0, 0);
+                }
+                ptx::fence_proxy_async_smem();  // before TMA overwrites this stage again
+                __syncwarp();
+            }
+
+            /* ---- S^T = K . Q^T : 16 tokens x 8 heads, K-dim = 128 ---- */
+            float sa[4] = {0.f, 0.f, 0.f, 0.f};
+            float sb[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks) {
+                const int half = ks >> 2;
+                const int ch = ((2 * ks) + (mj >> 1)) & 7;
+                const uint32_t addr = sK + half * kHalfBytes + tK * 128 + ((ch ^ mr) << 4);
+                uint32_t a0, a1, a2, a3;
+                ptx::ldsm_x4(addr, a0, a1, a2, a3);
+                if (ks & 1) ptx::mma_bf16_16816(sb, a0, a1, a2, a3, qf[2 * ks], qf[2 * ks + 1]);
+                else        ptx::mma_bf16_16816(sa, a0, a1, a2, a3, qf[2 * ks], qf[2 * ks + 1]);
+            }
+            // s[0]: (t=gid, h=2tig) s[1]: (gid, 2tig+1) s[2]: (gid+8, 2tig) s[3]: (gid+8, 2tig+1)
+            float s[4];
+#pragma unroll
+            for (int r = 0; r < 4; ++r) s[r] = (sa[r] + sb[r]) * p.scale_log2;
+            if (nvalid < kChunkTokens) {
+                if (gid >= nvalid) { s[0] = -INFINITY; s[1] = -INFINITY; }
+                if (gid + 8 >= nvalid) { s[2] = -INFINITY; s[3] = -INFINITY; }
+            }
+
+            /* ---- online softmax (log2 domain), heads hA = 2tig, hB = 2tig+1 ---- */
+            float mxA = fmaxf(s[0], s[2]);
+            float mxB = fmaxf(s[1], s[3]);
+#pragma unroll
+            for (int off = 4; off < 32; off <<= 1) {
+                mxA = fmaxf(mxA, __shfl_xor_sync(0xffffffffu, mxA, off));
+                mxB = fmaxf(mxB, __shfl_xor_sync(0xffffffffu, mxB, off));
+            }
+            const float mnA = fmaxf(m2[0], mxA);
+            const float mnB = fmaxf(m2[1], mxB);
+            const float alA = ptx::ex2(m2[0] - mnA);
+            const float alB = ptx::ex2(m2[1] - mnB);
+            m2[0] = mnA;
+            m2[1] = mnB;
+            const float p0 = ptx::ex2(s[0] - mnA);
+            const float p1 = ptx::ex2(s[1] - mnB);
+            const float p2 = ptx::ex2(s[2] - mnA);
+            const float p3 = ptx::ex2(s[3] - mnB);
+            l2[0] = fmaf(l2[0], alA, p0 + p2);
+            l2[1] = fmaf(l2[1], alB, p1 + p3);
+#pragma unroll
+            for (int mt = 0; mt < 8; ++mt) {
+                o[mt][0] *= alA; o[mt][1] *= alB; o[mt][2] *= alA; o[mt][3] *= alB;
+            }
+            /* P^T (tokens x heads) C-fragment -> B-fragment of the PV MMA. */
+            const uint32_t pb0 = ptx::movmatrix_t(ptx::pack_bf16x2(p0, p1));
+            const uint32_t pb1 = ptx::movmatrix_t(ptx::pack_bf16x2(p2, p3));
+
+            /* ---- O^T += V^T . P^T : 128 dims (8 M tiles) x 8 heads, K-dim = 16 tokens ---- */
+#pragma unroll
+            for (int mt = 0; mt < 8; ++mt) {
+                const int half = mt >> 2;
+                const int ch = ((2 * mt) + (mj & 1)) & 7;
+                const uint32_t addr = sV + half * kHalfBytes + tV * 128 + ((ch ^ mr) << 4);
+                uint32_t a0, a1, a2, a3;
+                ptx::ldsm_x4_t(addr, a0, a1, a2, a3);
+                ptx::mma_bf16_16816(o[mt], a0, a1, a2, a3, pb0, pb1);
+            }
+            __syncwarp();
+            if (issued < ntot) issue_next();  // refills the stage just consumed
+
+            const bool last_of_warp = (i == ntot - 1);
+            if (last_of_unit || last_of_warp) {
+                /* ---- finish this warp's part of the unit ---- */
+                float lA = l2[0], lB = l2[1];
+#pragma unroll
+                for (int off = 4; off < 32; off <<= 1) {
+                    lA += __shfl_xor_sync(0xffffffffu, lA, off);
+                    lB += __shfl_xor_sync(0xffffffffu, lB, off);
+                }
+                const float invA = 1.f / lA, invB = 1.f / lB;
+                const bool full = unit_start_seen && last_of_unit;
+                if (full) {
+                    const int32_t kvh = cc.j / p.n_hg;
+                    const int32_t hg = cc.j - kvh * p.n_hg;
+                    __nv_bfloat16* orow =
+                        p.out + ((int64_t)cc.b * p.Hq + kvh * p.g + hg * kHeadsPerGroup + gid) * kHeadDim;
+#pragma unroll
+                    for (int mt = 0; mt < 8; ++mt) {
+                        const uint32_t y0 = ptx::movmatrix_t(ptx::pack_bf16x2(o[mt][0] * invA, o[mt][1] * invB));
+                        const uint32_t y1 = ptx::movmatrix_t(ptx::pack_bf16x2(o[mt][2] * invA, o[mt][3] * invB));
+                        if (gid < nh_valid) {
+                            *reinterpret_cast<uint32_t*>(orow + mt * 16 + 2 * tig) = y0;
+                            *reinterpret_cast<uint32_t*>(orow + mt * 16 + 8 + 2 * tig) = y1;
+                        }
+                    }
+                } else {
+                    const float lseA = m2[0] + ptx::lg2(lA);
+                    const float lseB = m2[1] + ptx::lg2(lB);
+                    if (units_done == 0) {
+#pragma unroll
+                        for (int mt = 0; mt < 8; ++mt) {
+                            fo[mt][0] = o[mt][0] * invA; fo[mt][1] = o[mt][1] * invB;
+                            fo[mt][2] = o[mt][2] * invA; fo[mt][3] = o[mt][3] * invB;
+                        }
+                        flse[0] = lseA; flse[1] = lseB;
+                        first_u = cc;
+                        have_first = true;
+                    } else {
+                        // Only the warp's last unit can be cut at its end: keep it in place.
+#pragma unroll
+                        for (int mt = 0; mt < 8; ++mt) {
+                            o[mt][0] *= invA; o[mt][1] *= invB; o[mt][2] *= invA; o[mt][3] *= invB;
+                        }
+                        m2[0] = lseA; m2[1] = lseB;
+                        last_u = cc;
+                        have_last = true;
+                    }
+                }
+                ++units_done;
+                if (!last_of_warp) {
+                    advance(p, pre, cc);
+                    load_q(cc);
+                    reset_state();
+                    unit_start_seen = true;
+                }
+            } else {
+                ++cc.c;
+            }
+        }
+    }
+
+    /* ---- CTA level: stash cut units, merge across warps ---- */
+    __syncthreads();  // every warp has finished with its ring; reuse it for stashes
+    if (warp < W) {
+        Stash& s0 = stash[warp * 2 + 0];
+        Stash& s1 = stash[warp * 2 + 1];
+        const bool v0 = (warp < wa) && have_first && !aborted;
+        const bool v1 = (warp < wa) && have_last && !aborted;
+        if (v0) {
+#pragma unroll
+            for (int mt = 0; mt < 8; ++mt) {
+                s0.o[2 * tig][mt * 16 + gid] = fo[mt][0];
+                s0.o[2 * tig + 1][mt * 16 + gid] = fo[mt][1];
+                s0.o[2 * tig][mt * 16 + gid + 8] = fo[mt][2];
+                s0.o[2 * tig + 1][mt * 16 + gid + 8] = fo[mt][3];
+            }
+            if (gid == 0) { s0.lse[2 * tig] = flse[0]; s0.lse[2 * tig + 1] = flse[1]; }
+        }
+        if (v1) {
+#pragma unroll
+            for (int mt = 0; mt < 8; ++mt) {
+                s1.o[2 * tig][mt * 16 + gid] = o[mt][0];
+                s1.o[2 * tig + 1][mt * 16 + gid] = o[mt][1];
+                s1.o[2 * tig][mt * 16 + gid + 8] = o[mt][2];
+                s1.o[2 * tig + 1][mt * 16 + gid + 8] = o[mt][3];
+            }
+            if (gid == 0) { s1.lse[2 * tig] = m2[0]; s1.lse[2 * tig + 1] = m2[1]; }
+        }
+        if (lane == 0) {
+            s0.valid = v0; s0.b = first_u.b; s0.j = first_u.j;
+            s1.valid = v1; s1.b = last_u.b; s1.j = last_u.j;
+        }
+    }
+    __syncthreads();
+
+    if (warp < wa) {
+        const int d0 = lane * 4;
+#pragma unroll 1
+        for (int sidx = 0; sidx < 2; ++sidx) {
+            const Stash& me = stash[warp * 2 + sidx];
+            if (!me.valid) continue;
+            const int32_t ub = me.b, uj = me.j;
+            // Is this warp the last contributor inside the CTA?
+            if (warp + 1 < wa) {
+                const Stash& nx = stash[(warp + 1) * 2];
+                if (nx.valid && nx.b == ub && nx.j == uj) continue;
+            }
+            MergeAcc acc[8];
+#pragma unroll
+            for (int h = 0; h < 8; ++h) acc[h].init();
+#pragma unroll
+            for (int h = 0; h < 8; ++h)
+                acc[h].add(me.lse[h], *reinterpret_cast<const float4*>(&me.o[h][d0]));
+            if (sidx == 0) {
+                // u is this warp's first unit: earlier warps of the CTA may hold its head.
+                for (int k = warp - 1; k >= 0; --k) {
+                    const Stash& c1 = stash[k * 2 + 1];
+                    const Stash& c0 = stash[k * 2 + 0];
+                    const bool in1 = c1.valid && c1.b == ub && c1.j == uj;
+                    const bool in0 = c0.valid && c0.b == ub && c0.j == uj;
+                    const Stash* st = in1 ? &c1 : (in0 ? &c0 : nullptr);
+                    if (st == nullptr) break;
+#pragma unroll
+                    for (int h = 0; h < 8; ++h)
+                        acc[h].add(st->lse[h], *reinterpret_cast<const float4*>(&st->o[h][d0]));
+                    if (in1) break;  // u began inside warp k
+                }
+            }
+            const int32_t n_u = (int32_t)(pre[ub + 1] - pre[ub]);
+            const int64_t ubeg = unit_begin(p, pre, ub, uj);
+            const int32_t kvh = uj / p.n_hg;
+            const int32_t hg = uj - kvh * p.n_hg;
+            const int nhv = min(kHeadsPerGroup, p.g - hg * kHeadsPerGroup);
+            if (ubeg >= cs && ubeg + n_u <= ce) {
+                // Unit lies inside this CTA: final output.
+                __nv_bfloat16* orow = p.out + ((int64_t)ub * p.Hq + kvh * p.g + hg * kHeadsPerGroup) * kHeadDim;
+                for (int h = 0; h < nhv; ++h) {
+                    const float inv = 1.f / acc[h].den;
+                    store_bf16x4(orow + h * kHeadDim + d0, acc[h].a[0] * inv, acc[h].a[1] * inv,
+                                 acc[h].a[2] * inv, acc[h].a[3] * inv);
+                }
+            } else {
+                // Unit crosses the CTA boundary: write this CTA's record, count arrivals.
+                const int64_t slot = record_slot(blockIdx.x, cs, ubeg);
+                float* ro = p.rec_o + slot * (8 * kHeadDim);
+#pragma unroll
+                for (int h = 0; h < 8; ++h) {
+                    const float inv = 1.f / acc[h].den;
+                    *reinterpret_cast<float4*>(ro + h * kHeadDim + d0) =
+                        make_float4(acc[h].a[0] * inv, acc[h].a[1] * inv, acc[h].a[2] * inv,
+                                    acc[h].a[3] * inv);
+                }
+                if (lane < 8) {
+                    float lse = 0.f;
+#pragma unroll
+                    for (int h = 0; h < 8; ++h)
+                        if (h == lane) lse = acc[h].m + ptx::lg2(acc[h].den);
+                    p.rec_lse[slot * 8 + lane] = lse;
+                }
+                __threadfence();
+                __syncwarp();
+                if (lane == 0) {
+                    const int64_t c_first = slice_owner(ubeg, nct, T);
+                    const int64_t c_last = slice_owner(ubeg + n_u - 1, nct, T);
+                    const int32_t need = (int32_t)(c_last - c_first + 1);
+                    int32_t* cnt = p.counters + (int64_t)ub * p.U + uj;
+                    const int32_t prev = atomicAdd(cnt, 1);
+                    if (prev == need - 1) {
+                        *cnt = 0;  // leave the workspace zeroed for the next call
+                        __threadfence();
+                        const int fs = (slot & 1) ? 1 : 0;
+                        misc[8 + fs] = ub;
+                        misc[10 + fs] = uj;
+                    }
+                }
+            }
+        }
+    }
+    __syncthreads();
+
+    /* ---- global merge of units whose last record this CTA wrote ---- */
+#pragma unroll 1
+    for (int fs = 0; fs < 2; ++fs) {
+        const int32_t ub = misc[8 + fs];
+        if (ub < 0) continue;
+        const int32_t uj = misc[10 + fs];
+        const int32_t n_u = (int32_t)(pre[ub + 1] - pre[ub]);
+        const int64_t ubeg = unit_begin(p, pre, ub, uj);
+        const int64_t c_first = slice_owner(ubeg, nct, T);
+        const int64_t c_last = slice_owner(ubeg + n_u - 1, nct, T);
+        const int32_t kvh = uj / p.n_hg;
+        const int32_t hg = uj - kvh * p.n_hg;
+        const int nhv = min(kHeadsPerGroup, p.g - hg * kHeadsPerGroup);
+        // Thread layout: TPH threads per head, each covering 128/TPH dims in float4 pieces.
+        constexpr int TPH = NT / 8;
+        constexpr int EPT = kHeadDim / TPH;  // floats per thread (16 for W=1 ... 4 for W=8)
+        const int h = tid / TPH;
+        const int dbase = (tid % TPH) * EPT;
+        MergeAcc acc[EPT / 4];
+#pragma unroll
+        for (int e = 0; e < EPT / 4; ++e) acc[e].init();
+        for (int64_t c = c_first; c <= c_last; ++c) {
+            const int64_t slot = record_slot(c, slice_begin(c, nct, T), ubeg);
+            const float lse = __ldcg(p.rec_lse + slot * 8 + h);
+            const float* ro = p.rec_o + slot * (8 * kHeadDim) + h * kHeadDim + dbase;
+#pragma unroll
+            for (int e = 0; e < EPT / 4; ++e)
+                acc[e].add(lse, __ldcg(reinterpret_cast<const float4*>(ro) + e));
+        }
+        if (h < nhv) {
+            __nv_bfloat16* orow =
+                p.out + ((int64_t)ub * p.Hq + kvh * p.g + hg * kHeadsPerGroup + h) * kHeadDim + dbase;
+#pragma unroll
+            for (int e = 0; e < EPT / 4; ++e) {
+                const float inv = 1.f / acc[e].den;
+                store_bf16x4(orow + 4 * e, acc[e].a[0] * inv, acc[e].a[1] * inv, acc[e].a[2] * inv,
+                             acc[e].a[3] * inv);
+            }
+        }
+    }
+}
+
+/* ------------------------------------------------------------------------------------ */
+/* Host side                                                                            */
+/* ------------------------------------------------------------------------------------ */
+
+namespace {
+
+thread_local int g_last_status = PGQA_OK;
+
+int set_status(int s) {
+    g_last_status = s;
+    return s;
+}
+
+struct Variant {
+    int warps, stages;
+};
+
+int env_int(const char* name, int dflt) {
+    const char* v = getenv(name);
+    if (v == nullptr || *v == 0) return dflt;
+    return atoi(v);
+}
+
+/* Sweep knobs (unset in normal use): PGQA_WARPS, PGQA_STAGES, PGQA_MIN_CHUNKS, PGQA_GRID. */
+struct Knobs {
+    int warps, stages, min_chunks, grid;
+};
+const Knobs& knobs() {
+    static const Knobs k = {env_int("PGQA_WARPS", 0), env_int("PGQA_STAGES", 0),
+                            env_int("PGQA_MIN_CHUNKS", 0), env_int("PGQA_GRID", 0)};
+    return k;
+}
+
+constexpr int kDefaultWarps = 4;
+constexpr int kDefaultStages = 6;
+constexpr int kDefaultMinChunks = 4;
+constexpr int kB200Sms = 148;
+constexpr int kB200SmemOptin = 232448;
+
+size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+int smem_bytes_for(int warps, int stages, int64_t B) {
+    size_t s = 1024;  // alignment slack for the 1024-byte aligned ring
+    s += (size_t)warps * stages * kStageBytes;
+    s += (size_t)warps * stages * 8;
+    s += 32 * 4;
+    s += align_up((size_t)(B + 1) * 4, 16);
+    // The stash area reuses the ring; it must fit.
+    const size_t stash = (size_t)warps * 2 * sizeof(Stash);
+    if (stash > (size_t)warps * stages * kStageBytes) s += stash;
+    return (int)s;
+}
+
+bool variant_compiled(int w, int s) {
+    return (w == 4 && (s >= 3 && s <= 6)) || (w == 8 && (s == 2 || s == 3));
+}
+
+int validate_shape(int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int64_t P) {
+    if (B <= 0 || Hq <= 0 || Hkv <= 0 || D <= 0 || P <= 0) return PGQA_ERR_BAD_SHAPE;
+    if (Hq % Hkv != 0) return PGQA_ERR_BAD_SHAPE;
+    if (D != kHeadDim) return PGQA_ERR_UNSUPPORTED;
+    if (P % kChunkTokens != 0) return PGQA_ERR_UNSUPPORTED;
+    if (B > (1 << 24) || Hq > 4096) return PGQA_ERR_UNSUPPORTED;
+    return PGQA_OK;
+}
+
+int64_t workspace_bytes_for(int64_t B, int64_t U, int grid) {
+    size_t s = 256;                                   // error word (+ pad)
+    s += align_up((size_t)B * U * 4, 256);            // counters
+    s += align_up((size_t)2 * grid * 8 * 4, 256);     // record lse
+    s += align_up((size_t)2 * grid * 8 * kHeadDim * 4, 256);  // record o
+    return (int64_t)s;
+}
+
+int make_plan_impl(int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int64_t P, int sms,
+                   int smem_optin, pgqa_plan* plan) {
+    memset(plan, 0, sizeof(*plan));
+    const int st = validate_shape(B, Hq, Hkv, D, P);
+    plan->status = st;
+    if (st != PGQA_OK) return st;
+    if (sms <= 0) sms = kB200Sms;
+    if (smem_optin <= 0) smem_optin = kB200SmemOptin;
+    const int64_t g = Hq / Hkv;
+    const int64_t n_hg = ceil_div64(g, kHeadsPerGroup);
+    const Knobs& kn = knobs();
+    int w = kn.warps > 0 ? kn.warps : kDefaultWarps;
+    int s = kn.stages > 0 ? kn.stages : (w == 8 ? 3 : kDefaultStages);
+    if (!variant_compiled(w, s)) {
+        plan->status = PGQA_ERR_UNSUPPORTED;
+        return plan->status;
+    }
+    // Deepest ring that fits next to the per-sequence prefix table.
+    while (smem_bytes_for(w, s, B) > smem_optin && variant_compiled(w, s - 1)) --s;
+    if (smem_bytes_for(w, s, B) > smem_optin) {
+        plan->status = PGQA_ERR_UNSUPPORTED;  // batch too large for the in-CTA prefix table
+        return plan->status;
+    }
+    plan->warps_per_cta = w;
+    plan->stages = s;
+    plan->grid_ctas = kn.grid > 0 ? kn.grid : sms;
+    plan->min_chunks_per_warp = kn.min_chunks > 0 ? kn.min_chunks : kDefaultMinChunks;
+    plan->head_groups = (int32_t)n_hg;
+    plan->units_per_seq = (int32_t)(Hkv * n_hg);
+    plan->smem_bytes = smem_bytes_for(w, s, B);
+    plan->workspace_bytes = workspace_bytes_for(B, Hkv * n_hg, plan->grid_ctas);
+    plan->status = PGQA_OK;
+    return PGQA_OK;
+}
+
+/* ---- device properties, cached per device ---- */
+struct DevInfo {
+    bool init = false;
+    int status = PGQA_OK;
+    int sms = 0, smem_optin = 0;
+};
+constexpr int kMaxDevices = 64;
+DevInfo g_dev[kMaxDevices];
+std::mutex g_dev_mu;
+
+int device_info(int dev, DevInfo* out) {
+    if (dev < 0 || dev >= kMaxDevices) return PGQA_ERR_NO_DEVICE;
+    std::lock_guard<std::mutex> lk(g_dev_mu);
+    DevInfo& d = g_dev[dev];
+    if (!d.init) {
+        cudaDeviceProp prop;
+        if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) {
+            cudaGetLastError();
+            d.status = PGQA_ERR_NO_DEVICE;
+        } else if (prop.major != 10) {
+            d.status = PGQA_ERR_NO_DEVICE;  // built for sm_100a only
+        } else {
+            d.sms = prop.multiProcessorCount;
+            d.smem_optin = (int)prop.sharedMemPerBlockOptin;
+            d.status = PGQA_OK;
+        }
+        d.init = true;
+    }
+    *out = d;
+    return d.status;
+}
+
+/* ---- cuTensorMapEncodeTiled through the runtime's driver entry point ---- */
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, []() {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess) {
+            fn = reinterpret_cast<EncodeTiledFn>(ptr);
+        } else {
+            cudaGetLastError();
+        }
+    });
+    return fn;
+}
+
+/* Tensor map over one pool viewed as (d: 128, kv: Hkv, token: num_pages*P), box
+ * (64, 1, 16), 128-byte swizzle.  Out-of-range boxes read zeros (no fault). */
+int encode_pool_map(CUtensorMap* map, const void* base, int64_t Hkv, int64_t tokens) {
+    EncodeTiledFn fn = encode_fn();
+    if (fn == nullptr) return PGQA_ERR_CUDA;
+    cuuint64_t dims[3] = {(cuuint64_t)kHeadDim, (cuuint64_t)Hkv, (cuuint64_t)tokens};
+    cuuint64_t strides[2] = {(cuuint64_t)kHeadDim * 2, (cuuint64_t)(Hkv * kHeadDim * 2)};
+    cuuint32_t box[3] = {64, 1, (cuuint32_t)kChunkTokens};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims,
+                    strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? PGQA_OK : PGQA_ERR_CUDA;
+}
+
+/* ---- per-device library workspace for run_kernel ---- */
+struct LibWorkspace {
+    void* ptr = nullptr;
+    size_t bytes = 0;
+};
+LibWorkspace g_ws[kMaxDevices];
+std::mutex g_ws_mu;
+
+int lib_workspace(int dev, size_t need, void** out) {
+    std::lock_guard<std::mutex> lk(g_ws_mu);
+    LibWorkspace& w = g_ws[dev];
+    if (w.ptr == nullptr || w.bytes < need) {
+        if (w.ptr != nullptr) {
+            cudaDeviceSynchronize();
+            cudaFree(w.ptr);
+            w.ptr = nullptr;
+            w.bytes = 0;
+        }
+        size_t sz = need < ((size_t)4 << 20) ? ((size_t)4 << 20) : need;
+        if (cudaMalloc(&w.ptr, sz) != cudaSuccess) {
+            cudaGetLastError();
+            w.ptr = nullptr;
+            return PGQA_ERR_WORKSPACE;
+        }
+        if (cudaMemset(w.ptr, 0, sz) != cudaSuccess) {
+            cudaGetLastError();
+            return PGQA_ERR_CUDA;
+        }
+        w.bytes = sz;
+    }
+    *out = w.ptr;
+    return PGQA_OK;
+}
+
+template <int W, int S>
+int launch_variant(const CUtensorMap& km, const CUtensorMap& vm, const DecodeParams& p, int grid,
+                   int smem, cudaStream_t stream) {
+    auto kern = pgqa_decode_kernel<W, S>;
+    static int configured_smem[kMaxDevices] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (configured_smem[dev] < smem) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+            cudaSuccess) {
+            cudaGetLastError();
+            return PGQA_ERR_CUDA;
+        }
+        configured_smem[dev] = smem;
+    }
+    kern<<<grid, W * 32, smem, stream>>>(km, vm, p);
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? PGQA_OK : PGQA_ERR_CUDA;
+}
+
+int launch(const pgqa_plan& plan, const CUtensorMap& km, const CUtensorMap& vm,
+           const DecodeParams& p, cudaStream_t stream) {
+    const int w = plan.warps_per_cta, s = plan.stages;
+    const int g = plan.grid_ctas, sm = plan.smem_bytes;
+    if (w == 4 && s == 6) return launch_variant<4, 6>(km, vm, p, g, sm, stream);
+    if (w == 4 && s == 5) return launch_variant<4, 5>(km, vm, p, g, sm, stream);
+    if (w == 4 && s == 4) return launch_variant<4, 4>(km, vm, p, g, sm, stream);
+    if (w == 4 && s == 3) return launch_variant<4, 3>(km, vm, p, g, sm, stream);
+    if (w == 8 && s == 3) return launch_variant<8, 3>(km, vm, p, g, sm, stream);
+    if (w == 8 && s == 2) return launch_variant<8, 2>(km, vm, p, g, sm, stream);
+    return PGQA_ERR_UNSUPPORTED;
+}
+
+int decode_impl(const void* q, const void* k, const void* v, void* out, const int32_t* seq_lens,
+                const int32_t* bt, int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int64_t P,
+                int64_t num_pages, int64_t bt_stride, int64_t max_seqlen, float scale,
+                void* workspace, size_t ws_bytes, cudaStream_t stream) {
+    if (!q || !k || !v || !out || !seq_lens || !bt) return PGQA_ERR_NULL_POINTER;
+    int st = validate_shape(B, Hq, Hkv, D, P);
+    if (st != PGQA_OK) return st;
+    if (num_pages <= 0 || bt_stride <= 0) return PGQA_ERR_BAD_SHAPE;
+    if (num_pages * P >= ((int64_t)1 << 31)) return PGQA_ERR_UNSUPPORTED;
+    const int64_t cap = bt_stride * P;
+    if (max_seqlen < 0 || max_seqlen > cap) return PGQA_ERR_BAD_SHAPE;
+    if (!(scale > 0.f) || !isfinite(scale)) return PGQA_ERR_BAD_SHAPE;
+    if ((reinterpret_cast<uintptr_t>(k) & 15) || (reinterpret_cast<uintptr_t>(v) & 15) ||
+        (reinterpret_cast<uintptr_t>(q) & 15) || (reinterpret_cast<uintptr_t>(out) & 15) ||
+        (reinterpret_cast<uintptr_t>(seq_lens) & 3) || (reinterpret_cast<uintptr_t>(bt) & 3))
+        return PGQA_ERR_MISALIGNED;
+
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        cudaGetLastError();
+        return PGQA_ERR_NO_DEVICE;
+    }
+    DevInfo di;
+    st = device_info(dev, &di);
+    if (st != PGQA_OK) return st;
+    pgqa_plan plan;
+    st = make_plan_impl(B, Hq, Hkv, D, P, di.sms, di.smem_optin, &plan);
+    if (st != PGQA_OK) return st;
+
+    if (workspace == nullptr) {
+        st = lib_workspace(dev, (size_t)plan.workspace_bytes, &workspace);
+        if (st != PGQA_OK) return st;
+    } else if (ws_bytes < (size_t)plan.workspace_bytes) {
+        return PGQA_ERR_WORKSPACE;
+    }
+    if (reinterpret_cast<uintptr_t>(workspace) & 255) return PGQA_ERR_MISALIGNED;
+
+    CUtensorMap km, vm;
+    st = encode_pool_map(&km, k, Hkv, num_pages * P);
+    if (st != PGQA_OK) return st;
+    st = encode_pool_map(&vm, v, Hkv, num_pages * P);
+    if (st != PGQA_OK) return st;
+
+    const int64_t g = Hq / Hkv;
+    DecodeParams p;
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    p.err = reinterpret_cast<int32_t*>(ws);
+    size_t off = 256;
+    p.counters = reinterpret_cast<int32_t*>(ws + off);
+    off += align_up((size_t)B * plan.units_per_seq * 4, 256);
+    p.rec_lse = reinterpret_cast<float*>(ws + off);
+    off += align_up((size_t)2 * plan.grid_ctas * 8 * 4, 256);
+    p.rec_o = reinterpret_cast<float*>(ws + off);
+    p.q = static_cast<const __nv_bfloat16*>(q);
+    p.out = static_cast<__nv_bfloat16*>(out);
+    p.seq_lens = seq_lens;
+    p.block_table = bt;
+    p.B = (int32_t)B;
+    p.Hq = (int32_t)Hq;
+    p.Hkv = (int32_t)Hkv;
+    p.g = (int32_t)g;
+    p.n_hg = plan.head_groups;
+    p.U = plan.units_per_seq;
+    p.page_size = (int32_t)P;
+    p.bt_stride = (int32_t)bt_stride;
+    p.num_pages = (int32_t)num_pages;
+    p.cap_tokens = cap;
+    p.scale_log2 = scale * 1.4426950408889634f;
+    p.min_chunks = plan.min_chunks_per_warp;
+    // Test hooks, read per call: PGQA_DEBUG_STUCK_BARRIER=1 makes one stage barrier wait
+    // for 16 bytes that never arrive (its wait expires -> PGQA_ERR_DEVICE_TIMEOUT);
+    // PGQA_WAIT_LIMIT_NS shortens the bound on every wait.
+    p.debug_stuck = env_int("PGQA_DEBUG_STUCK_BARRIER", 0) != 0;
+    {
+        const char* lim = getenv("PGQA_WAIT_LIMIT_NS");
+        p.wait_limit_ns = (lim && *lim) ? strtoull(lim, nullptr, 10) : kWaitLimitNs;
+        if (p.wait_limit_ns == 0 || p.wait_limit_ns > 10 * kWaitLimitNs) p.wait_limit_ns = kWaitLimitNs;
+    }
+    return launch(plan, km, vm, p, stream);
+}
+
+}  // namespace
+}  // namespace pgqa
+
+/* ------------------------------------------------------------------------------------ */
+/* C ABI                                                                                */
+/* ------------------------------------------------------------------------------------ */
+
+using namespace pgqa;
+
+extern "C" void run_kernel(const void* q, const void* k_cache_paged, const void* v_cache_paged,
+                           void* output, const int32_t* cache_seqlens,
+                           const int32_t* block_table, int64_t batch_size, int64_t seqlen_k,
+                           int64_t seqlen_q, int64_t num_heads, int64_t num_heads_k,
+                           int64_t headdim, int64_t page_block_size, int64_t num_blocks,
+                           int64_t causal) {
+    if (batch_size <= 0 || num_blocks <= 0 || num_blocks % batch_size != 0 || seqlen_k < 0 ||
+        page_block_size <= 0) {
+        set_status(PGQA_ERR_BAD_SHAPE);
+        return;
+    }
+    // One query token: a causal mask aligned to the sequence end hides nothing, so
+    // causal = 0 and causal = 1 give the same result.
+    if (seqlen_q != 1 || (causal != 0 && causal != 1)) {
+        set_status(PGQA_ERR_UNSUPPORTED);
+        return;
+    }
+    const int64_t stride = num_blocks / batch_size;
+    if (seqlen_k > stride * page_block_size) {
+        set_status(PGQA_ERR_BAD_SHAPE);
+        return;
+    }
+    const float scale = 1.0f / sqrtf((float)headdim);
+    set_status(decode_impl(q, k_cache_paged, v_cache_paged, output, cache_seqlens, block_table,
+                           batch_size, num_heads, num_heads_k, headdim, page_block_size,
+                           num_blocks, stride, seqlen_k, scale, nullptr, 0, (cudaStream_t)0));
+}
+
+extern "C" int pgqa_decode_v1(const void* q, const void* k_cache, const void* v_cache, void* out,
+                              const int32_t* seq_lens, const int32_t* block_table,
+                              int64_t batch_size, int64_t num_heads, int64_t num_heads_k,
+                              int64_t headdim, int64_t page_size, int64_t num_pages,
+                              int64_t bt_stride, int64_t max_seqlen, float scale,
+                              void* workspace, size_t workspace_bytes, void* stream) {
+    return set_status(decode_impl(q, k_cache, v_cache, out, seq_lens, block_table, batch_size,
+                                  num_heads, num_heads_k, headdim, page_size, num_pages, bt_stride,
+                                  max_seqlen, scale, workspace, workspace_bytes,
+                                  static_cast<cudaStream_t>(stream)));
+}
+
+extern "C" size_t pgqa_workspace_size(int64_t batch_size, int64_t num_heads, int64_t num_heads_k,
+                                      int64_t headdim, int64_t page_size) {
+    int sms = 0, optin = 0;
+    int dev = 0;
+    DevInfo di;
+    if (cudaGetDevice(&dev) == cudaSuccess && device_info(dev, &di) == PGQA_OK) {
+        sms = di.sms;
+        optin = di.smem_optin;
+    } else {
+        cudaGetLastError();
+    }
+    pgqa_plan plan;
+    if (make_plan_impl(batch_size, num_heads, num_heads_k, headdim, page_size, sms, optin, &plan) !=
+        PGQA_OK)
+        return 0;
+    return (size_t)plan.workspace_bytes;
+}
+
+extern "C" int pgqa_workspace_init(void* workspace, size_t workspace_bytes, void* stream) {
+    if (workspace == nullptr) return set_status(PGQA_ERR_NULL_POINTER);
+    if (cudaMemsetAsync(workspace, 0, workspace_bytes, static_cast<cudaStream_t>(stream)) !=
+        cudaSuccess) {
+        cudaGetLastError();
+        return set_status(PGQA_ERR_CUDA);
+    }
+    return set_status(PGQA_OK);
+}
+
+extern "C" int pgqa_last_status(void) { return g_last_status; }
+
+extern "C" const char* pgqa_status_string(int status) {
+    switch (status) {
+        case PGQA_OK: return "ok";
+        case PGQA_ERR_NULL_POINTER: return "null pointer argument";
+        case PGQA_ERR_BAD_SHAPE: return "invalid shape argument";
+        case PGQA_ERR_UNSUPPORTED: return "unsupported configuration";
+        case PGQA_ERR_MISALIGNED: return "misaligned pointer";
+        case PGQA_ERR_WORKSPACE: return "workspace missing, too small or not allocatable";
+        case PGQA_ERR_CUDA: return "CUDA call failed";
+        case PGQA_ERR_NO_DEVICE: return "no usable sm_100 device";
+        case PGQA_ERR_DEVICE_TIMEOUT: return "device-side wait timed out";
+        case PGQA_ERR_DEVICE_BAD_PAGE: return "block_table entry outside [0, num_pages)";
+        case PGQA_ERR_DEVICE_BAD_SEQLEN: return "seq_len outside [0, table capacity]";
+        default: return "unknown status";
+    }
+}
+
+extern "C" int pgqa_check_device_error(void* workspace, void* stream) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        cudaGetLastError();
+        return PGQA_ERR_NO_DEVICE;
+    }
+    if (workspace == nullptr) {
+        std::lock_guard<std::mutex> lk(g_ws_mu);
+        if (dev < 0 || dev >= kMaxDevices || g_ws[dev].ptr == nullptr) return PGQA_OK;
+        workspace = g_ws[dev].ptr;
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    int32_t word = 0;
+    if (cudaMemcpyAsync(&word, workspace, 4, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+        cudaStreamSynchronize(s) != cudaSuccess) {
+        cudaGetLastError();
+        return PGQA_ERR_CUDA;
+    }
+    if (word != 0) {
+        cudaMemsetAsync(workspace, 0, 4, s);
+        cudaStreamSynchronize(s);
+    }
+    if (word & kErrTimeout) return PGQA_ERR_DEVICE_TIMEOUT;
+    if (word & kErrBadPage) return PGQA_ERR_DEVICE_BAD_PAGE;
+    if (word & kErrBadSeqlen) return PGQA_ERR_DEVICE_BAD_SEQLEN;
+    return PGQA_OK;
+}
+
+extern "C" int pgqa_make_plan(int64_t batch_size, int64_t num_heads, int64_t num_heads_k,
+                              int64_t headdim, int64_t page_size, int32_t num_sms,
+                              int32_t smem_per_block_optin, pgqa_plan* plan) {
+    if (plan == nullptr) return PGQA_ERR_NULL_POINTER;
+    return make_plan_impl(batch_size, num_heads, num_heads_k, headdim, page_size, num_sms,
+                          smem_per_block_optin, plan);
+}
+
+extern "C" int64_t pgqa_simulate_partition(const int32_t* seq_lens, int64_t B, int64_t U,
+                                           int64_t cap_tokens, const pgqa_plan* plan,
+                                           int32_t* ctas_per_unit, int32_t* segments_per_unit) {
+    if (!seq_lens || !plan || !ctas_per_unit || !segments_per_unit) return -PGQA_ERR_NULL_POINTER;
+    if (B <= 0 || U <= 0 || plan->grid_ctas <= 0 || plan->warps_per_cta <= 0) return -PGQA_ERR_BAD_SHAPE;
+    int64_t* pre = static_cast<int64_t*>(malloc(sizeof(int64_t) * (B + 1)));
+    if (!pre) return -PGQA_ERR_WORKSPACE;
+    pre[0] = 0;
+    for (int64_t b = 0; b < B; ++b) pre[b + 1] = pre[b] + seq_chunks(seq_lens[b], cap_tokens);
+    for (int64_t u = 0; u < B * U; ++u) ctas_per_unit[u] = segments_per_unit[u] = 0;
+    const int64_t T = pre[B] * U;
+    if (T == 0) {
+        free(pre);
+        return 0;
+    }
+    auto unit_of = [&](int64_t x) -> int64_t {  // flat unit index containing chunk x
+        int64_t lo = 0, hi = B;
+        while (hi - lo > 1) {
+            const int64_t mid = (lo + hi) / 2;
+            if (pre[mid] * U <= x) lo = mid; else hi = mid;
+        }
+        const int64_t n = pre[lo + 1] - pre[lo];
+        return lo * U + (x - pre[lo] * U) / n;
+    };
+    const int64_t W = plan->warps_per_cta;
+    const int64_t nct = active_ctas(T, plan->grid_ctas, W, plan->min_chunks_per_warp);
+    for (int64_t c = 0; c < nct; ++c) {
+        const int64_t cs = slice_begin(c, nct, T), ce = slice_begin(c + 1, nct, T);
+        for (int64_t u = unit_of(cs); u <= unit_of(ce - 1); ++u) ctas_per_unit[u] += 1;
+        const int64_t len = ce - cs;
+        const int64_t wa = active_warps(len, W);
+        for (int64_t w = 0; w < wa; ++w) {
+            const int64_t ws = cs + slice_begin(w, wa, len), we = cs + slice_begin(w + 1, wa, len);
+            for (int64_t u = unit_of(ws); u <= unit_of(we - 1); ++u) segments_per_unit[u] += 1;
+        }
+    }
+    free(pre);
+    return nct;
+}
+
+extern "C" const char* pgqa_version(void) { return "pgqa-b200 0.1 (sm_100a)"; }

@@ -1,0 +1,81 @@
+/*
+ * Work partition of the paged-GQA decode, shared by the device kernel and the host
+ * simulation (pgqa_simulate_partition), so the CPU tests check the exact
+ * arithmetic the GPU runs.
+ *
+ * The reference splits each (batch, kv_head) unit into `ns` equal page ranges, with
+ * ns picked from seven hand-tuned regimes on the *capacity* seqlen_k
+ * (submission_clean.cu:375-430, :453-461), and lets splits beyond a sequence's real
+ * length exit early (:93).  Here the work is instead measured in 16-token chunks
+ * of the *actual* lengths and cut into equal contiguous slices:
+ *
+ *   unit u = (b, j), j in [0, units_per_seq) = (kv_head, head_group), b-major;
+ *   unit (b, j) owns n_b = ceil(L_b / 16) chunks;
+ *   flat chunk index of chunk c of unit (b, j) = pre[b] * U + j * n_b + c,
+ *   where pre[b] = sum_{b' < b} n_b' and U = units_per_seq;
+ *   T = pre[B] * U chunks in total.
+ *
+ * Active CTA i of n owns flat chunks [i*T/n, (i+1)*T/n); inside it, warp k of w owns
+ * the k-th of w equal sub-slices.  Every chunk is owned by exactly one warp, every
+ * warp gets the same number of chunks (+-1), and the number of pieces a unit is
+ * cut into follows from its length, B*Hkv and the SM count.
+ */
+#ifndef PGQA_PARTITION_H_
+#define PGQA_PARTITION_H_
+
+#include <stdint.h>
+
+#if defined(__CUDACC__)
+#define PGQA_HD __host__ __device__ __forceinline__
+#else
+#define PGQA_HD inline
+#endif
+
+namespace pgqa {
+
+constexpr int kChunkTokens = 16;   // tokens per pipeline stage / MMA M tile
+constexpr int kHeadDim = 128;      // the only head dimension compiled
+constexpr int kHeadsPerGroup = 8;  // query heads per MMA N tile
+
+PGQA_HD int64_t ceil_div64(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+/* Chunks of a sequence of `len` valid tokens (clamped to [0, cap]). */
+PGQA_HD int64_t seq_chunks(int64_t len, int64_t cap_tokens) {
+    if (len < 0) len = 0;
+    if (len > cap_tokens) len = cap_tokens;
+    return ceil_div64(len, kChunkTokens);
+}
+
+/* Start of slice i when [0, total) is cut into n equal contiguous slices. */
+PGQA_HD int64_t slice_begin(int64_t i, int64_t n, int64_t total) {
+    return (i * total) / n;
+}
+
+/* Index of the slice that contains position x (0 <= x < total). */
+PGQA_HD int64_t slice_owner(int64_t x, int64_t n, int64_t total) {
+    return ((x + 1) * n - 1) / total;
+}
+
+/* Number of active CTAs for `total` chunks: every active warp gets at least
+ * `min_chunks` chunks unless the whole problem is smaller than one CTA's share. */
+PGQA_HD int64_t active_ctas(int64_t total, int64_t grid, int64_t warps, int64_t min_chunks) {
+    int64_t n = total / (warps * min_chunks);
+    if (n > grid) n = grid;
+    if (n < 1) n = 1;
+    return n;
+}
+
+/* Active warps of a CTA whose slice holds `len` chunks. */
+PGQA_HD int64_t active_warps(int64_t len, int64_t warps) {
+    return len < warps ? len : warps;
+}
+
+/* Global record slot of CTA c for unit starting at flat chunk `unit_begin`:
+ * 2c when the unit contains the CTA's first chunk, else 2c+1. */
+PGQA_HD int64_t record_slot(int64_t c, int64_t cta_begin, int64_t unit_begin) {
+    return unit_begin <= cta_begin ? 2 * c : 2 * c + 1;
+}
+
+}  // namespace pgqa
+
+#endif  // PGQA_PARTITION_H_

@@ -1,0 +1,147 @@
+"""Tensor-level entry points over the C ABI.
+
+`run_kernel` mirrors the reference's Python operator surface
+(submission_c500_regions.py:979-995: q, k_cache_paged, v_cache_paged, output,
+cache_seqlens, block_table and the nine integer arguments of the C `run_kernel`,
+task.md:33-54) with the same argument meaning: the block-table row width is
+num_blocks / batch_size, the pool has num_blocks pages and the scale is 1/sqrt(headdim).
+It launches on torch's current stream.
+
+`decode` is the general form (explicit scale, any pool size / table stride).
+
+Both run only the CUDA library: a missing or non-sm_100 device raises.
+"""
+import ctypes
+import math
+
+import torch
+
+from ._lib import PgqaError, PgqaPlan, check, lib
+
+_workspaces = {}
+
+
+def _ptr(t):
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def _stream_handle(device):
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def workspace_for(batch_size, num_heads, num_heads_k, headdim, page_size, device):
+    """A zero-initialised workspace tensor for pgqa_decode_v1, cached per device/shape."""
+    L = lib()
+    dev = torch.device(device)
+    with torch.cuda.device(dev):
+        need = L.pgqa_workspace_size(batch_size, num_heads, num_heads_k, headdim, page_size)
+    if need == 0:
+        raise PgqaError(2, "pgqa_workspace_size")
+    key = (dev.index, need)
+    ws = _workspaces.get(dev.index)
+    if ws is None or ws.numel() < need:
+        ws = torch.zeros(max(need, 1 << 20), dtype=torch.uint8, device=dev)
+        _workspaces[dev.index] = ws
+    return ws
+
+
+def _check_tensors(q, k, v, out, seq_lens, block_table):
+    for name, t, dt in (("q", q, torch.bfloat16), ("k", k, torch.bfloat16),
+                        ("v", v, torch.bfloat16), ("out", out, torch.bfloat16),
+                        ("seq_lens", seq_lens, torch.int32),
+                        ("block_table", block_table, torch.int32)):
+        if not t.is_cuda:
+            raise ValueError(f"{name} must be a CUDA tensor")
+        if t.dtype != dt:
+            raise TypeError(f"{name} must be {dt}, got {t.dtype}")
+        if not t.is_contiguous():
+            raise ValueError(f"{name} must be contiguous")
+
+
+def decode(q, k_cache, v_cache, block_table, seq_lens, scale=None, out=None,
+           max_seqlen=0, workspace=None):
+    """Paged GQA decode.
+
+    q [B, Hq, D] or [B, 1, Hq, D]; k_cache/v_cache [num_pages, P, Hkv, D] (bf16);
+    block_table [B, stride] int32; seq_lens [B] int32.  Returns out (same shape as q).
+    """
+    if out is None:
+        out = torch.empty_like(q)
+    _check_tensors(q, k_cache, v_cache, out, seq_lens, block_table)
+    B = q.shape[0]
+    Hq, D = q.shape[-2], q.shape[-1]
+    if q.dim() == 4 and q.shape[1] != 1:
+        raise PgqaError(3, "decode: seqlen_q must be 1")
+    num_pages, P, Hkv, Dk = k_cache.shape
+    if tuple(v_cache.shape) != tuple(k_cache.shape) or Dk != D:
+        raise PgqaError(2, "decode: K/V pool shapes")
+    if block_table.dim() != 2 or block_table.shape[0] != B or seq_lens.shape != (B,):
+        raise PgqaError(2, "decode: block_table / seq_lens shapes")
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    if workspace is None:
+        workspace = workspace_for(B, Hq, Hkv, D, P, q.device)
+    L = lib()
+    with torch.cuda.device(q.device):
+        st = L.pgqa_decode_v1(_ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(out), _ptr(seq_lens),
+                              _ptr(block_table), B, Hq, Hkv, D, P, num_pages,
+                              block_table.stride(0), max_seqlen, float(scale),
+                              _ptr(workspace), workspace.numel(), _stream_handle(q.device))
+    check(st, "pgqa_decode_v1")
+    return out
+
+
+def run_kernel(q, k_cache_paged, v_cache_paged, output, cache_seqlens, block_table,
+               batch_size, seqlen_k, seqlen_q, num_heads, num_heads_k, headdim,
+               page_block_size, num_blocks, causal):
+    """Reference operator surface (tensors + the C run_kernel integers)."""
+    batch_size, num_blocks = int(batch_size), int(num_blocks)
+    if batch_size <= 0 or num_blocks % batch_size != 0:
+        raise PgqaError(2, "run_kernel: num_blocks must be a multiple of batch_size")
+    if int(seqlen_q) != 1 or int(causal) not in (0, 1):
+        raise PgqaError(3, "run_kernel: only seqlen_q == 1 decode is supported")
+    stride = num_blocks // batch_size
+    if int(seqlen_k) > stride * int(page_block_size):
+        raise PgqaError(2, "run_kernel: seqlen_k exceeds the block-table capacity")
+    q3 = q.view(batch_size, int(num_heads), int(headdim))
+    o3 = output.view(batch_size, int(num_heads), int(headdim))
+    k = k_cache_paged.view(num_blocks, int(page_block_size), int(num_heads_k), int(headdim))
+    v = v_cache_paged.view(num_blocks, int(page_block_size), int(num_heads_k), int(headdim))
+    bt = block_table.view(batch_size, stride)
+    decode(q3, k, v, bt, cache_seqlens, scale=1.0 / math.sqrt(int(headdim)), out=o3,
+           max_seqlen=int(seqlen_k))
+    return output
+
+
+def run_kernel_cabi(q, k_cache_paged, v_cache_paged, output, cache_seqlens, block_table,
+                    batch_size, seqlen_k, seqlen_q, num_heads, num_heads_k, headdim,
+                    page_block_size, num_blocks, causal):
+    """Calls the C `run_kernel` symbol exactly as the reference harness does
+    (verify_real.py:12-14,32-38: ctypes, 6 pointers + 9 int64, legacy default stream)."""
+    L = lib()
+    with torch.cuda.device(q.device):
+        L.run_kernel(_ptr(q), _ptr(k_cache_paged), _ptr(v_cache_paged), _ptr(output),
+                     _ptr(cache_seqlens), _ptr(block_table), int(batch_size), int(seqlen_k),
+                     int(seqlen_q), int(num_heads), int(num_heads_k), int(headdim),
+                     int(page_block_size), int(num_blocks), int(causal))
+        st = L.pgqa_last_status()
+    check(st, "run_kernel")
+    return output
+
+
+def check_device_error(workspace=None, device=None):
+    """Synchronously read and clear the device error word (raises on error)."""
+    L = lib()
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    with torch.cuda.device(dev):
+        ptr = _ptr(workspace) if workspace is not None else None
+        st = L.pgqa_check_device_error(ptr, _stream_handle(dev))
+    check(st, "device error word")
+
+
+def make_plan(batch_size, num_heads, num_heads_k, headdim, page_size, num_sms=0,
+              smem_optin=0):
+    plan = PgqaPlan()
+    st = lib().pgqa_make_plan(batch_size, num_heads, num_heads_k, headdim, page_size,
+                              num_sms, smem_optin, ctypes.byref(plan))
+    return st, plan

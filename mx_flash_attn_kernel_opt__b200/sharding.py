@@ -1,0 +1,42 @@
+"""KV-head sharding of the decode across GPUs (one process per GPU).
+
+The op splits by KV head with no exchange step: rank r of N owns KV heads
+[r*Hkv/N, (r+1)*Hkv/N), their K/V pool (its own allocation, [num_pages, P, Hkv/N, D]) and
+query heads [r*Hq/N, (r+1)*Hq/N); block_table and seq_lens are replicated.  Each rank
+runs the single-GPU decode on its shard.  Assembling the full [B, Hq, D] output is an
+optional all-gather over the process group (NCCL on GPUs), timed separately from the
+decode.
+"""
+import torch
+import torch.distributed as dist
+
+
+def kv_head_range(rank, world_size, num_heads_k):
+    if num_heads_k % world_size != 0:
+        raise ValueError(f"num_heads_k={num_heads_k} is not divisible by {world_size} ranks")
+    per = num_heads_k // world_size
+    return rank * per, (rank + 1) * per
+
+
+def q_head_range(rank, world_size, num_heads, num_heads_k):
+    lo, hi = kv_head_range(rank, world_size, num_heads_k)
+    g = num_heads // num_heads_k
+    return lo * g, hi * g
+
+
+def shard_tensors(q, k_cache, v_cache, rank, world_size):
+    """Slices a full problem into rank `rank`'s shard (copies; used by tests)."""
+    Hkv = k_cache.shape[2]
+    lo, hi = kv_head_range(rank, world_size, Hkv)
+    qlo, qhi = q_head_range(rank, world_size, q.shape[-2], Hkv)
+    return (q[..., qlo:qhi, :].contiguous(), k_cache[:, :, lo:hi].contiguous(),
+            v_cache[:, :, lo:hi].contiguous())
+
+
+def gather_heads(out_local, group=None):
+    """All-gather every rank's [B, Hq/N, D] output into the full [B, Hq, D]."""
+    world = dist.get_world_size(group)
+    B, hq_local, D = out_local.shape
+    buf = torch.empty((world * B, hq_local, D), dtype=out_local.dtype, device=out_local.device)
+    dist.all_gather_into_tensor(buf, out_local.contiguous(), group=group)
+    return buf.view(world, B, hq_local, D).permute(1, 0, 2, 3).reshape(B, world * hq_local, D)

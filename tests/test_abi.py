@@ -1,0 +1,128 @@
+"""The C ABI: libpgqa.so loads, exports every symbol include/pgqa.h declares, and
+validates its arguments on the host (no GPU needed)."""
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+import torch
+
+from mx_flash_attn_kernel_opt__b200 import _lib, make_plan
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(REPO, "include", "pgqa.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    names = re.findall(r"^[A-Za-z_][\w \*]*?\b([A-Za-z_]\w*)\s*\(", text, flags=re.M)
+    return sorted(set(n for n in names if n not in ("if", "while")))
+
+
+def test_header_declares_the_reference_symbol():
+    names = declared_functions()
+    assert "run_kernel" in names
+    assert {"pgqa_decode_v1", "pgqa_workspace_size", "pgqa_make_plan"} <= set(names)
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    L = _lib.lib()
+    for name in declared_functions():
+        assert hasattr(L, name), name
+        assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
+    out = subprocess.run(["nm", "-D", "--defined-only", _lib.LIB_PATH], capture_output=True,
+                         text=True).stdout
+    exported = set(line.split()[-1] for line in out.splitlines() if " T " in line)
+    for name in declared_functions():
+        assert name in exported, name
+
+
+def test_status_strings():
+    L = _lib.lib()
+    for code in _lib.STATUS:
+        assert L.pgqa_status_string(code).decode() != "unknown status"
+    assert L.pgqa_status_string(999).decode() == "unknown status"
+    assert L.pgqa_version().decode().startswith("pgqa-b200")
+
+
+@pytest.mark.parametrize("shape", [(4, 32, 8, 16), (2, 64, 8, 16), (256, 32, 8, 16),
+                                   (64, 28, 4, 64), (512, 64, 8, 16), (8, 32, 4, 16)])
+def test_plan_for_benchmark_shapes(shape):
+    B, Hq, Hkv, P = shape
+    st, plan = make_plan(B, Hq, Hkv, 128, P)
+    assert st == 0 and plan.status == 0
+    assert plan.grid_ctas == 148
+    assert plan.smem_bytes <= 232448
+    assert plan.stages >= 3
+    assert plan.head_groups == -(-(Hq // Hkv) // 8)
+    assert plan.workspace_bytes > 0
+
+
+def test_plan_rejects_bad_shapes():
+    assert make_plan(0, 32, 8, 128, 16)[0] == 2
+    assert make_plan(4, 30, 8, 128, 16)[0] == 2      # Hq % Hkv != 0
+    assert make_plan(4, 32, 8, 64, 16)[0] == 3       # D != 128
+    assert make_plan(4, 32, 8, 128, 8)[0] == 3       # page size not a multiple of 16
+    st, plan = make_plan(4, 32, 8, 128, 16, num_sms=132, smem_optin=232448)
+    assert st == 0 and plan.grid_ctas == 132
+
+
+def test_plan_shrinks_ring_for_large_batches():
+    _, small = make_plan(8, 32, 8, 128, 16)
+    _, big = make_plan(20000, 32, 8, 128, 16)
+    assert big.status == 0 and big.stages < small.stages and big.smem_bytes <= 232448
+
+
+FAKE = ctypes.c_void_p(0x10000)
+
+
+def _v1(**kw):
+    a = dict(q=FAKE, k=FAKE, v=FAKE, out=FAKE, sl=FAKE, bt=FAKE, B=4, Hq=32, Hkv=8, D=128,
+             P=16, num_pages=64, stride=16, max_seqlen=256, scale=0.088, ws=None, wsb=0,
+             stream=None)
+    a.update(kw)
+    return _lib.lib().pgqa_decode_v1(a["q"], a["k"], a["v"], a["out"], a["sl"], a["bt"], a["B"],
+                                     a["Hq"], a["Hkv"], a["D"], a["P"], a["num_pages"],
+                                     a["stride"], a["max_seqlen"], a["scale"], a["ws"],
+                                     a["wsb"], a["stream"])
+
+
+def test_extended_entry_validates_arguments():
+    assert _v1(q=None) == 1
+    assert _v1(B=0) == 2
+    assert _v1(Hq=31) == 2
+    assert _v1(D=256) == 3
+    assert _v1(P=24) == 3
+    assert _v1(num_pages=0) == 2
+    assert _v1(max_seqlen=10**6) == 2          # above stride * page_size
+    assert _v1(scale=-1.0) == 2
+    assert _v1(k=ctypes.c_void_p(0x10008)) == 4  # TMA base must be 16-byte aligned
+    assert _lib.lib().pgqa_last_status() == 4
+
+
+@pytest.mark.skipif(torch.cuda.is_available(), reason="checks the no-device path")
+def test_valid_call_without_device_reports_no_device():
+    assert _v1() == 7
+
+
+def test_reference_entry_validates_arguments():
+    L = _lib.lib()
+    args = [FAKE] * 6
+    L.run_kernel(*args, 0, 16, 1, 32, 8, 128, 16, 64, 0)
+    assert L.pgqa_last_status() == 2              # batch_size 0
+    L.run_kernel(*args, 4, 16, 1, 32, 8, 128, 16, 63, 0)
+    assert L.pgqa_last_status() == 2              # num_blocks % batch_size
+    L.run_kernel(*args, 4, 16, 2, 32, 8, 128, 16, 64, 0)
+    assert L.pgqa_last_status() == 3              # seqlen_q != 1
+    L.run_kernel(*args, 4, 1000, 1, 32, 8, 128, 16, 64, 0)
+    assert L.pgqa_last_status() == 2              # seqlen_k above table capacity
+    L.run_kernel(*args, 4, 16, 1, 32, 8, 96, 16, 64, 0)
+    assert L.pgqa_last_status() == 3              # headdim
+
+
+def test_workspace_size_is_zero_for_invalid_shapes():
+    L = _lib.lib()
+    assert L.pgqa_workspace_size(0, 32, 8, 128, 16) == 0
+    assert L.pgqa_workspace_size(4, 32, 8, 128, 16) > 0

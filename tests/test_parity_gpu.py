@@ -1,0 +1,246 @@
+"""GPU parity of the CUDA decode against the reference's golden vectors and the CPU oracle.
+
+Acceptance, per case:
+  * the reference's rule (verify_real.py:42-45): >= 99% of elements within
+    1.6e-2 + 1.6e-2*|ref| (100% for its edge cases 1-3) and none beyond 8x that; and
+  * every element within atol = rtol = 1e-2 of the fp32 oracle (torch.allclose);
+  * block-table indexing bit-exact: pools poisoned with NaN in every slot a correct
+    kernel must not read still give finite, matching outputs.
+"""
+import math
+import os
+
+import pytest
+import torch
+
+import mx_flash_attn_kernel_opt__b200 as pgqa
+from mx_flash_attn_kernel_opt__b200 import _lib, inputs, ops
+from oracle import match_stats, paged_decode_ref
+from tests._golden import CASES, is_edge, load_rows, make_inputs
+
+pytestmark = pytest.mark.gpu
+
+ATOL = RTOL = 1e-2
+
+
+def assert_parity(out, ref, edge=False, what=""):
+    out = out.float().cpu()
+    ref = ref.float().cpu()
+    assert torch.isfinite(out).all(), f"{what}: non-finite output"
+    frac, outlier, maxd = match_stats(out, ref)
+    assert not outlier, f"{what}: 8x-tolerance outlier (max |diff| {maxd})"
+    assert frac >= (1.0 if edge else 0.99), f"{what}: match ratio {frac}"
+    assert torch.allclose(out, ref, atol=ATOL, rtol=RTOL), f"{what}: max |diff| {maxd}"
+
+
+def run_cabi(inp, dev):
+    d = inp.to(dev)
+    out = torch.zeros_like(d.q)
+    B, Hq, D = d.q.shape
+    pgqa.run_kernel_cabi(d.q, d.k, d.v, out, d.seq_lens, d.block_table, B, inp.seqlen_k, 1,
+                         Hq, inp.num_heads_k, D, inp.page_size, inp.num_pages, 0)
+    torch.cuda.synchronize(dev)
+    pgqa.check_device_error()
+    return out
+
+
+def run_v1(inp, dev, **kw):
+    d = inp.to(dev)
+    out = pgqa.decode(d.q, d.k, d.v, d.block_table, d.seq_lens, scale=inp.scale, **kw)
+    torch.cuda.synchronize(dev)
+    return out
+
+
+# ---- the reference's own outputs ----------------------------------------------------
+
+@pytest.mark.parametrize("name", sorted(CASES))
+def test_golden_case_through_reference_symbol(name, cuda_device):
+    entry = CASES[name]
+    inp = make_inputs(entry["spec"])
+    assert inp.digest() == entry["digest"]
+    out = run_cabi(inp, cuda_device)
+    rows, gold = load_rows(name)
+    assert_parity(out[rows], gold, edge=is_edge(name), what=f"{name} vs reference output")
+    ref = paged_decode_ref(inp.q, inp.k, inp.v, inp.block_table, inp.seq_lens)
+    assert_parity(out, ref, edge=is_edge(name), what=f"{name} vs oracle")
+
+
+def test_python_operator_surface_matches_c_symbol(cuda_device):
+    inp = inputs.spj_case(6, table="permuted")
+    a = run_cabi(inp, cuda_device)
+    d = inp.to(cuda_device)
+    b = torch.zeros(d.batch, 1, d.num_heads, 128, dtype=torch.bfloat16, device=cuda_device)
+    pgqa.run_kernel(d.q.view(d.batch, 1, d.num_heads, 128), d.k, d.v, b, d.seq_lens,
+                    d.block_table, d.batch, inp.seqlen_k, 1, d.num_heads, d.num_heads_k, 128,
+                    d.page_size, d.num_pages, 0)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b.view_as(a))
+
+
+# ---- the benchmark workloads ------------------------------------------------------
+
+@pytest.mark.parametrize("name", ["c1", "c2", "c3", "c4"])
+def test_baseline_config_vs_oracle(name, cuda_device):
+    inp = inputs.baseline_config(name)
+    out = run_v1(inp, cuda_device)
+    ref = paged_decode_ref(inp.q, inp.k, inp.v, inp.block_table, inp.seq_lens)
+    assert_parity(out, ref, what=name)
+
+
+def test_c5_full_size_sampled_rows_and_page_permutation(cuda_device):
+    """c5 at full size (~34 GB): sampled sequences against the oracle, and bit-identical
+    output after moving every page to another physical slot (indexing is exact)."""
+    dev = cuda_device
+    inp = inputs.baseline_config("c5", device=dev)
+    out = pgqa.decode(inp.q, inp.k, inp.v, inp.block_table, inp.seq_lens, scale=inp.scale)
+    torch.cuda.synchronize()
+    rows = [0, 1, 255, 511]
+    P = inp.page_size
+    for b in rows:
+        L = int(inp.seq_lens[b])
+        ids = inp.block_table[b, :(L + P - 1) // P].to(torch.int64)
+        sub = inputs.DecodeInputs(
+            q=inp.q[b:b + 1].cpu(), k=inp.k.index_select(0, ids).cpu(),
+            v=inp.v.index_select(0, ids).cpu(),
+            block_table=torch.arange(len(ids), dtype=torch.int32).view(1, -1),
+            seq_lens=inp.seq_lens[b:b + 1].cpu(), scale=inp.scale)
+        ref = paged_decode_ref(sub.q, sub.k, sub.v, sub.block_table, sub.seq_lens)
+        assert_parity(out[b:b + 1], ref, what=f"c5 row {b}")
+    # permute physical pages: new_k[perm[i]] = k[i], table entries mapped through perm
+    g = torch.Generator(device="cpu")
+    g.manual_seed(11)
+    perm = torch.randperm(inp.num_pages, generator=g).to(dev)
+    k2 = torch.empty_like(inp.k)
+    k2[perm] = inp.k
+    del inp.k
+    torch.cuda.empty_cache()
+    v2 = torch.empty_like(inp.v)
+    v2[perm] = inp.v
+    del inp.v
+    torch.cuda.empty_cache()
+    bt2 = perm.to(torch.int32)[inp.block_table.to(torch.int64)]
+    out2 = pgqa.decode(inp.q, k2, v2, bt2, inp.seq_lens, scale=inp.scale)
+    torch.cuda.synchronize()
+    assert torch.equal(out, out2)
+
+
+# ---- edges: lengths, page sizes, group sizes, poisoned pools ------------------------
+
+@pytest.mark.parametrize("P", [16, 32, 64, 128])
+@pytest.mark.parametrize("Hq,Hkv", [(32, 8), (32, 4), (28, 4), (8, 8), (16, 1), (64, 2),
+                                    (24, 3), (6, 2)])
+def test_edge_lengths_poisoned(P, Hq, Hkv, cuda_device):
+    lens = [1, 2, 15, 16, 17, P - 1, P, P + 1, 2 * P + 3, 100, 1000, 31, 33]
+    width = max((L + P - 1) // P for L in lens) + 2
+    inp = inputs.custom_case(len(lens), Hq, Hkv, P, lens, seed=P * 100 + Hq, width=width,
+                             spare_pages=7)
+    ref = paged_decode_ref(inp.q, inp.k, inp.v, inp.block_table, inp.seq_lens)
+    out = run_v1(inputs.poison(inp), cuda_device)
+    assert_parity(out, ref, edge=True, what=f"P={P} Hq={Hq} Hkv={Hkv}")
+
+
+def test_zero_length_sequences_give_zeros(cuda_device):
+    inp = inputs.custom_case(4, 32, 8, 16, [0, 40, 0, 3], seed=9, width=4)
+    out = run_v1(inp, cuda_device)
+    ref = paged_decode_ref(inp.q, inp.k, inp.v, inp.block_table, inp.seq_lens)
+    assert torch.count_nonzero(out[0]) == 0 and torch.count_nonzero(out[2]) == 0
+    assert_parity(out, ref, edge=True, what="zero lengths")
+
+
+@pytest.mark.parametrize("lens", [[1], [16], [5000], [1] * 300, [2048, 1, 1, 7, 65536]])
+def test_extreme_batches(lens, cuda_device):
+    inp = inputs.custom_case(len(lens), 32, 4, 16, lens, seed=len(lens))
+    out = run_v1(inp, cuda_device)
+    ref = paged_decode_ref(inp.q, inp.k, inp.v, inp.block_table, inp.seq_lens)
+    assert_parity(out, ref, what=f"lens={lens[:5]}")
+
+
+def test_repeated_calls_are_bit_identical(cuda_device):
+    """The fused combine's arrival counters must be left at zero by every call."""
+    inp = inputs.baseline_config("c3").to(cuda_device)
+    outs = [pgqa.decode(inp.q, inp.k, inp.v, inp.block_table, inp.seq_lens, scale=inp.scale)
+            for _ in range(3)]
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[1], outs[2])
+
+
+def test_caller_workspace_on_side_stream(cuda_device):
+    inp = inputs.spj_case(11, table="permuted")
+    d = inp.to(cuda_device)
+    L = _lib.lib()
+    need = L.pgqa_workspace_size(d.batch, d.num_heads, d.num_heads_k, 128, d.page_size)
+    ws = torch.empty(need, dtype=torch.uint8, device=cuda_device)
+    side = torch.cuda.Stream(cuda_device)
+    with torch.cuda.stream(side):
+        assert L.pgqa_workspace_init(ops._ptr(ws), need, ops._stream_handle(cuda_device)) == 0
+        out = pgqa.decode(d.q, d.k, d.v, d.block_table, d.seq_lens, scale=inp.scale,
+                          workspace=ws)
+    side.synchronize()
+    pgqa.check_device_error(ws)
+    ref = paged_decode_ref(inp.q, inp.k, inp.v, inp.block_table, inp.seq_lens)
+    assert_parity(out, ref, what="side stream")
+    # a workspace that is too small is rejected before any launch
+    with pytest.raises(pgqa.PgqaError):
+        pgqa.decode(d.q, d.k, d.v, d.block_table, d.seq_lens, workspace=ws[:need // 2])
+
+
+def test_custom_scale(cuda_device):
+    inp = inputs.custom_case(3, 16, 2, 16, [7, 70, 700], seed=21)
+    d = inp.to(cuda_device)
+    out = pgqa.decode(d.q, d.k, d.v, d.block_table, d.seq_lens, scale=0.03)
+    ref = paged_decode_ref(inp.q, inp.k, inp.v, inp.block_table, inp.seq_lens, scale=0.03)
+    assert_parity(out, ref, what="scale 0.03")
+
+
+# ---- device error word --------------------------------------------------------------
+
+def _fresh_ws(inp, dev):
+    L = _lib.lib()
+    need = L.pgqa_workspace_size(inp.batch, inp.num_heads, inp.num_heads_k, 128, inp.page_size)
+    return torch.zeros(need, dtype=torch.uint8, device=dev)
+
+
+def test_bad_page_id_is_reported(cuda_device):
+    inp = inputs.custom_case(2, 32, 8, 16, [40, 20], seed=5, width=3)
+    bt = inp.block_table.clone()
+    bt[0, 1] = inp.num_pages + 5
+    d = inputs.DecodeInputs(q=inp.q, k=inp.k, v=inp.v, block_table=bt, seq_lens=inp.seq_lens,
+                            scale=inp.scale).to(cuda_device)
+    ws = _fresh_ws(inp, cuda_device)
+    pgqa.decode(d.q, d.k, d.v, d.block_table, d.seq_lens, workspace=ws)
+    with pytest.raises(pgqa.PgqaError) as e:
+        pgqa.check_device_error(ws)
+    assert e.value.status == 9
+    pgqa.check_device_error(ws)  # cleared
+
+
+def test_seq_len_above_capacity_is_reported(cuda_device):
+    inp = inputs.custom_case(2, 32, 8, 16, [40, 20], seed=6, width=3)
+    d = inp.to(cuda_device)
+    d.seq_lens[1] = 10 ** 6
+    ws = _fresh_ws(inp, cuda_device)
+    pgqa.decode(d.q, d.k, d.v, d.block_table, d.seq_lens, workspace=ws)
+    with pytest.raises(pgqa.PgqaError) as e:
+        pgqa.check_device_error(ws)
+    assert e.value.status == 10
+
+
+def test_expired_wait_reports_timeout_and_context_survives(cuda_device, monkeypatch):
+    """One stage barrier waits for 16 bytes nothing sends: its bounded wait expires, the
+    kernel records PGQA_ERR_DEVICE_TIMEOUT and returns; the context stays usable."""
+    inp = inputs.custom_case(2, 32, 8, 16, [300, 200], seed=8)
+    d = inp.to(cuda_device)
+    ws = _fresh_ws(inp, cuda_device)
+    monkeypatch.setenv("PGQA_DEBUG_STUCK_BARRIER", "1")
+    monkeypatch.setenv("PGQA_WAIT_LIMIT_NS", "20000000")
+    pgqa.decode(d.q, d.k, d.v, d.block_table, d.seq_lens, workspace=ws)
+    with pytest.raises(pgqa.PgqaError) as e:
+        pgqa.check_device_error(ws)
+    assert e.value.status == 8
+    monkeypatch.delenv("PGQA_DEBUG_STUCK_BARRIER")
+    monkeypatch.delenv("PGQA_WAIT_LIMIT_NS")
+    ws.zero_()  # a call that failed may leave arrival counters behind
+    out = pgqa.decode(d.q, d.k, d.v, d.block_table, d.seq_lens, workspace=ws)
+    pgqa.check_device_error(ws)
+    ref = paged_decode_ref(inp.q, inp.k, inp.v, inp.block_table, inp.seq_lens)
+    assert_parity(out, ref, what="after timeout")
