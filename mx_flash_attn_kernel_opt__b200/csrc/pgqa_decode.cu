@@ -182,10 +182,10 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
         ptx::prefetch_tensormap(&vmap);
         for (int i = 0; i < W * S; ++i) ptx::mbar_init(ptx::smem_u32(bars + i), 1);
         ptx::fence_mbar_init();
-        misc[8] = -1;  // global-merge flags for record slot 0 / 1 (unit b)
-        misc[9] = -1;  // (unit j)
-        misc[10] = -1;
-        misc[11] = -1;
+        misc[16] = -1;  // global-merge flags: unit b of record slot 0 / 1
+        misc[17] = -1;
+        misc[18] = -1;  // unit j of record slot 0 / 1
+        misc[19] = -1;
     }
 
     /* ---- chunk prefix over sequences (every CTA computes it; B is small) ---- */
@@ -289,7 +289,6 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
                 const int32_t z = pid * P + off;
                 const uint32_t extra =
                     (p.debug_stuck && blockIdx.x == 0 && warp == 0 && issued == 0) ? 16u : 0u;
-                ptx::fence_proxy_async_smem();
                 ptx::mbar_arrive_expect_tx(bar, kStageBytes + extra);
                 ptx::tma_load_3d(dst, &kmap, bar, 0, kvh, z, pol);
                 ptx::tma_load_3d(dst + kHalfBytes, &kmap, bar, 64, kvh, z, pol);
@@ -597,20 +596,20 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
                         if (h == lane) lse = acc[h].m + ptx::lg2(acc[h].den);
                     p.rec_lse[slot * 8 + lane] = lse;
                 }
-                __threadfence();
-                __syncwarp();
+                __syncwarp();  // the warp's record stores happen before lane 0's release
                 if (lane == 0) {
                     const int64_t c_first = slice_owner(ubeg, nct, T);
                     const int64_t c_last = slice_owner(ubeg + n_u - 1, nct, T);
                     const int32_t need = (int32_t)(c_last - c_first + 1);
                     int32_t* cnt = p.counters + (int64_t)ub * p.U + uj;
-                    const int32_t prev = atomicAdd(cnt, 1);
+                    ptx::fence_acq_rel_gpu();  // release this CTA's record
+                    const int32_t prev = ptx::atom_add_relaxed_gpu(cnt, 1);
                     if (prev == need - 1) {
+                        ptx::fence_acq_rel_gpu();  // acquire the other CTAs' records
                         *cnt = 0;  // leave the workspace zeroed for the next call
-                        __threadfence();
                         const int fs = (slot & 1) ? 1 : 0;
-                        misc[8 + fs] = ub;
-                        misc[10 + fs] = uj;
+                        misc[16 + fs] = ub;
+                        misc[18 + fs] = uj;
                     }
                 }
             }
@@ -618,43 +617,49 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
     }
     __syncthreads();
 
-    /* ---- global merge of units whose last record this CTA wrote ---- */
+    /* ---- global merge of units whose last record this CTA wrote ----
+     * One pass per (head, 4 dims) per thread: the lse and o of up to 8 records are
+     * loaded together (one L2 round trip), then folded with a running max. */
 #pragma unroll 1
     for (int fs = 0; fs < 2; ++fs) {
-        const int32_t ub = misc[8 + fs];
-        if (ub < 0) continue;
-        const int32_t uj = misc[10 + fs];
+        const int32_t ub = misc[16 + fs];
+        if (ub < 0) continue;  // same value in every thread of the CTA
+        const int32_t uj = misc[18 + fs];
         const int32_t n_u = (int32_t)(pre[ub + 1] - pre[ub]);
         const int64_t ubeg = unit_begin(p, pre, ub, uj);
         const int64_t c_first = slice_owner(ubeg, nct, T);
         const int64_t c_last = slice_owner(ubeg + n_u - 1, nct, T);
+        const int nrec = (int)(c_last - c_first + 1);
         const int32_t kvh = uj / p.n_hg;
         const int32_t hg = uj - kvh * p.n_hg;
         const int nhv = min(kHeadsPerGroup, p.g - hg * kHeadsPerGroup);
-        // Thread layout: TPH threads per head, each covering 128/TPH dims in float4 pieces.
-        constexpr int TPH = NT / 8;
-        constexpr int EPT = kHeadDim / TPH;  // floats per thread (16 for W=1 ... 4 for W=8)
-        const int h = tid / TPH;
-        const int dbase = (tid % TPH) * EPT;
-        MergeAcc acc[EPT / 4];
+        for (int idx = tid; idx < 8 * 32; idx += NT) {
+            const int h = idx >> 5;
+            const int d0 = (idx & 31) * 4;
+            MergeAcc acc;
+            acc.init();
+            for (int r0 = 0; r0 < nrec; r0 += 8) {
+                float lse[8];
+                float4 v[8];
 #pragma unroll
-        for (int e = 0; e < EPT / 4; ++e) acc[e].init();
-        for (int64_t c = c_first; c <= c_last; ++c) {
-            const int64_t slot = record_slot(c, slice_begin(c, nct, T), ubeg);
-            const float lse = __ldcg(p.rec_lse + slot * 8 + h);
-            const float* ro = p.rec_o + slot * (8 * kHeadDim) + h * kHeadDim + dbase;
+                for (int u = 0; u < 8; ++u) {
+                    if (r0 + u < nrec) {
+                        const int64_t c = c_first + r0 + u;
+                        const int64_t slot = record_slot(c, slice_begin(c, nct, T), ubeg);
+                        lse[u] = __ldcg(p.rec_lse + slot * 8 + h);
+                        v[u] = __ldcg(reinterpret_cast<const float4*>(
+                            p.rec_o + slot * (8 * kHeadDim) + h * kHeadDim + d0));
+                    }
+                }
 #pragma unroll
-            for (int e = 0; e < EPT / 4; ++e)
-                acc[e].add(lse, __ldcg(reinterpret_cast<const float4*>(ro) + e));
-        }
-        if (h < nhv) {
-            __nv_bfloat16* orow =
-                p.out + ((int64_t)ub * p.Hq + kvh * p.g + hg * kHeadsPerGroup + h) * kHeadDim + dbase;
-#pragma unroll
-            for (int e = 0; e < EPT / 4; ++e) {
-                const float inv = 1.f / acc[e].den;
-                store_bf16x4(orow + 4 * e, acc[e].a[0] * inv, acc[e].a[1] * inv, acc[e].a[2] * inv,
-                             acc[e].a[3] * inv);
+                for (int u = 0; u < 8; ++u)
+                    if (r0 + u < nrec) acc.add(lse[u], v[u]);
+            }
+            if (h < nhv) {
+                const float inv = 1.f / acc.den;
+                __nv_bfloat16* orow =
+                    p.out + ((int64_t)ub * p.Hq + kvh * p.g + hg * kHeadsPerGroup + h) * kHeadDim + d0;
+                store_bf16x4(orow, acc.a[0] * inv, acc.a[1] * inv, acc.a[2] * inv, acc.a[3] * inv);
             }
         }
     }
@@ -693,8 +698,8 @@ const Knobs& knobs() {
     return k;
 }
 
-constexpr int kDefaultWarps = 4;
-constexpr int kDefaultStages = 6;
+constexpr int kDefaultWarps = 8;
+constexpr int kDefaultStages = 3;
 constexpr int kDefaultMinChunks = 4;
 constexpr int kB200Sms = 148;
 constexpr int kB200SmemOptin = 232448;
@@ -726,11 +731,18 @@ int validate_shape(int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int64_t P) {
     return PGQA_OK;
 }
 
+/* Workspace layout: [error word | record lse | record o | arrival counters].  The record
+ * regions depend only on the grid, so the counters start at the same offset for every
+ * shape: a workspace reused across shapes never reads old records as counters. */
+size_t records_bytes(int grid) {
+    return align_up((size_t)2 * grid * 8 * 4, 256) +
+           align_up((size_t)2 * grid * 8 * kHeadDim * 4, 256);
+}
+
 int64_t workspace_bytes_for(int64_t B, int64_t U, int grid) {
     size_t s = 256;                                   // error word (+ pad)
-    s += align_up((size_t)B * U * 4, 256);            // counters
-    s += align_up((size_t)2 * grid * 8 * 4, 256);     // record lse
-    s += align_up((size_t)2 * grid * 8 * kHeadDim * 4, 256);  // record o
+    s += records_bytes(grid);                         // record lse + record o
+    s += align_up((size_t)B * U * 4, 256);            // arrival counters
     return (int64_t)s;
 }
 
@@ -746,7 +758,7 @@ int make_plan_impl(int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int64_t P, int
     const int64_t n_hg = ceil_div64(g, kHeadsPerGroup);
     const Knobs& kn = knobs();
     int w = kn.warps > 0 ? kn.warps : kDefaultWarps;
-    int s = kn.stages > 0 ? kn.stages : (w == 8 ? 3 : kDefaultStages);
+    int s = kn.stages > 0 ? kn.stages : (w == 4 ? 6 : kDefaultStages);
     if (!variant_compiled(w, s)) {
         plan->status = PGQA_ERR_UNSUPPORTED;
         return plan->status;
@@ -954,11 +966,11 @@ int decode_impl(const void* q, const void* k, const void* v, void* out, const in
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     p.err = reinterpret_cast<int32_t*>(ws);
     size_t off = 256;
-    p.counters = reinterpret_cast<int32_t*>(ws + off);
-    off += align_up((size_t)B * plan.units_per_seq * 4, 256);
     p.rec_lse = reinterpret_cast<float*>(ws + off);
     off += align_up((size_t)2 * plan.grid_ctas * 8 * 4, 256);
     p.rec_o = reinterpret_cast<float*>(ws + off);
+    off = 256 + records_bytes(plan.grid_ctas);
+    p.counters = reinterpret_cast<int32_t*>(ws + off);
     p.q = static_cast<const __nv_bfloat16*>(q);
     p.out = static_cast<__nv_bfloat16*>(out);
     p.seq_lens = seq_lens;

@@ -71,6 +71,21 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+/* GPU-scope acquire-release fence (lighter than the sequentially consistent
+ * fence __threadfence emits); pairs with relaxed atomics on arrival counters. */
+__device__ __forceinline__ void fence_acq_rel_gpu() {
+    asm volatile("fence.acq_rel.gpu;" ::: "memory");
+}
+
+__device__ __forceinline__ int32_t atom_add_relaxed_gpu(int32_t* ptr, int32_t v) {
+    int32_t old;
+    asm volatile("atom.add.relaxed.gpu.global.s32 %0, [%1], %2;"
+                 : "=r"(old)
+                 : "l"(ptr), "r"(v)
+                 : "memory");
+    return old;
+}
+
 __device__ __forceinline__ uint64_t policy_evict_first() {
     uint64_t pol;
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));

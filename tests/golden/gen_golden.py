@@ -4,9 +4,10 @@ The reference (dddd109/mx_flash_attn_kernel_opt_) ships one implementation of th
 that runs outside MetaX hardware: the Triton operator `run_kernel` of
 submission_c500_regions.py:979-1201 (same arguments as the C `run_kernel`).  This script
 imports it from a local checkout of the reference and runs it on the CPU under Triton's
-interpreter (TRITON_INTERPRET=1).  The interpreter computes `tl.dot` on raw bf16 bit
-patterns as integers, so `_patch_interpreter_bf16_dot` first makes it compute bf16 dots
-as exact fp32 products with fp32 accumulation (what a tensor core does).
+interpreter (TRITON_INTERPRET=1).  The interpreter stores bf16 as raw uint16 bit
+patterns and would compute on them as integers, so `_patch_interpreter_bf16` first makes
+it treat them as numbers (bf16 dots as exact fp32 products with fp32 accumulation, as a
+tensor core does; elementwise bf16 arithmetic and fp32 -> bf16 casts rounded to nearest).
 
 Inputs come from mx_flash_attn_kernel_opt__b200.inputs (seeded CPU generators, so the
 tests regenerate the same bytes; manifest.json records a sha256 of every input).  Only
@@ -26,27 +27,80 @@ REPO = os.path.dirname(os.path.dirname(HERE))
 ROWS_KEPT = 4
 
 
-def _patch_interpreter_bf16_dot():
+def _patch_interpreter_bf16():
+    """Make Triton's CPU interpreter treat bf16 (stored as raw uint16 bits) as numbers:
+    dots as exact fp32 products with fp32 accumulation, elementwise bf16 arithmetic in
+    fp32 rounded to nearest-even, fp32 -> bf16 casts rounded to nearest-even, and bf16
+    scalar constants (what the GPU lowering of these operations does)."""
     import numpy as np
+    import torch
     import triton.language as tl
     import triton.runtime.interpreter as interp
 
     cls = next(obj for name, obj in vars(interp).items()
                if isinstance(obj, type) and hasattr(obj, "create_dot"))
-    orig = cls.create_dot
+
+    def bits_to_f32(bits):
+        return (np.asarray(bits).astype(np.uint32) << 16).view(np.float32)
+
+    def f32_to_bits(x):
+        t = torch.from_numpy(np.ascontiguousarray(np.asarray(x, dtype=np.float32)))
+        return t.to(torch.bfloat16).view(torch.int16).numpy().astype(np.uint16)
 
     def to_f32(h):
         if h.dtype.scalar == tl.bfloat16:
-            return (h.data.astype(np.uint32) << 16).view(np.float32)
+            return bits_to_f32(h.data)
         return h.data.astype(np.float32)
+
+    orig_dot = cls.create_dot
 
     def create_dot(self, a, b, d, input_precision, max_num_imprecise_acc):
         if a.dtype.scalar == tl.bfloat16 or b.dtype.scalar == tl.bfloat16:
             prod = np.matmul(to_f32(a), to_f32(b), dtype=np.float32)
             return interp.TensorHandle(prod.astype(d.data.dtype) + d.data, d.dtype.scalar)
-        return orig(self, a, b, d, input_precision, max_num_imprecise_acc)
+        return orig_dot(self, a, b, d, input_precision, max_num_imprecise_acc)
+
+    orig_binary = cls.binary_op
+
+    def binary_op(self, lhs, rhs, op):
+        if lhs.dtype.scalar == tl.bfloat16 or rhs.dtype.scalar == tl.bfloat16:
+            res = op(to_f32(lhs), to_f32(rhs))
+            if res.dtype == np.bool_:
+                return interp.TensorHandle(res, tl.int1)
+            return interp.TensorHandle(f32_to_bits(res), tl.bfloat16)
+        return orig_binary(self, lhs, rhs, op)
+
+    orig_cast = cls.cast_impl
+
+    def cast_impl(self, src, dst_type):
+        if src.dtype.scalar == tl.float32 and dst_type.scalar == tl.bfloat16:
+            return interp.TensorHandle(f32_to_bits(src.data), tl.bfloat16)
+        return orig_cast(self, src, dst_type)
+
+    orig_fp2fp = cls.create_fp_to_fp
+
+    def create_fp_to_fp(self, src, dst_type, rounding_mode):
+        if src.dtype.scalar == tl.float32 and dst_type.scalar == tl.bfloat16:
+            return interp.TensorHandle(f32_to_bits(src.data), tl.bfloat16)
+        if src.dtype.scalar == tl.bfloat16 and dst_type.scalar == tl.float32:
+            return interp.TensorHandle(bits_to_f32(src.data), tl.float32)
+        return orig_fp2fp(self, src, dst_type, rounding_mode)
+
+    def get_bf16(self, value):
+        return interp.TensorHandle(f32_to_bits(np.array([value], dtype=np.float32)),
+                                   tl.bfloat16)
 
     cls.create_dot = create_dot
+    cls.binary_op = binary_op
+    for name in ("create_fadd", "create_fmul", "create_fdiv", "create_fsub", "create_frem",
+                 "create_precise_divf"):
+        op = {"create_fadd": np.add, "create_fmul": np.multiply, "create_fdiv": np.divide,
+              "create_fsub": np.subtract, "create_frem": np.fmod,
+              "create_precise_divf": np.divide}[name]
+        setattr(cls, name, (lambda o: (lambda self, l, r: self.binary_op(l, r, o)))(op))
+    cls.cast_impl = cast_impl
+    cls.create_fp_to_fp = create_fp_to_fp
+    cls.get_bf16 = get_bf16
 
 
 def cases():
@@ -83,7 +137,7 @@ def main():
     import torch
     import triton
 
-    _patch_interpreter_bf16_dot()
+    _patch_interpreter_bf16()
     sys.path.insert(0, args.reference)
     import submission_c500_regions as ref  # the reference's operator
 

@@ -99,7 +99,8 @@ def test_long_context_split_count_follows_sm_count():
     n, ctas, segs = simulate(seq.tolist(), plan.units_per_seq, cap, plan)
     assert n == 148
     assert set(ctas.tolist()) <= {9, 10, 11}
-    assert segs.sum() == 148 * plan.warps_per_cta + (segs.sum() - 148 * plan.warps_per_cta)
+    # every warp slice adds one piece, plus one per unit boundary crossed inside a slice
+    assert 148 * plan.warps_per_cta <= segs.sum() <= 148 * plan.warps_per_cta + len(segs)
     # with 4 SMs the same work is split 1-2 ways per unit
     st, small = make_plan(2, 64, 8, 128, 16, num_sms=4, smem_optin=232448)
     n4, ctas4, _ = simulate(seq.tolist(), small.units_per_seq, cap, small)
