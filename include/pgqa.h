@@ -43,7 +43,8 @@ enum pgqa_status {
     PGQA_ERR_NO_DEVICE = 7,         /* no usable CUDA device (or not sm_100)            */
     PGQA_ERR_DEVICE_TIMEOUT = 8,    /* a bounded device-side wait expired (device word) */
     PGQA_ERR_DEVICE_BAD_PAGE = 9,   /* a block-table entry was outside [0, num_pages)   */
-    PGQA_ERR_DEVICE_BAD_SEQLEN = 10 /* a seq_len was < 0 or above the table capacity    */
+    PGQA_ERR_DEVICE_BAD_SEQLEN = 10, /* a seq_len was < 0 or above the table capacity   */
+    PGQA_ERR_SCRATCH_LIMIT = 11     /* shape exceeds pgqa_decode_noalloc's fixed scratch */
 };
 
 /*
@@ -83,6 +84,33 @@ int pgqa_decode_v1(const void* q, const void* k_cache, const void* v_cache, void
                    int64_t page_size, int64_t num_pages, int64_t bt_stride,
                    int64_t max_seqlen, float scale, void* workspace, size_t workspace_bytes,
                    void* stream);
+
+/*
+ * Allocation-free variant of pgqa_decode_v1 (no counterpart in the reference).
+ *
+ * Some callers cannot allocate device memory when they call the decode: code running
+ * while a CUDA graph is being captured (cudaMalloc is not allowed there), serving
+ * engines that reserve nearly all of HBM in their own pool and allow no other
+ * allocation on the hot path (cudaMalloc may also synchronise the device), and
+ * plugin hosts that hand the operator only its input and output buffers.  This entry
+ * point takes the same arguments as pgqa_decode_v1 minus the workspace and allocates
+ * nothing: its scratch (split records and arrival counters) lives in a fixed 4 MiB
+ * device array inside the library, which every GPU that loads the library holds until
+ * the process exits.  Shapes needing more (about 740,000 sequence x KV-head units on a
+ * 148-SM B200) are rejected with PGQA_ERR_SCRATCH_LIMIT before anything is launched.
+ * The caller still passes q, the pools, seq_lens, block_table and out.
+ *
+ * The first call on a device looks up the array's device address (done once per
+ * device, with that device current); make that first call before any stream capture.
+ * Each call clears the parts of the array that must start at zero.  All calls share
+ * the one array, so calls that overlap on the GPU (different streams, or different
+ * host threads) race and give wrong results: order them on one stream.
+ */
+int pgqa_decode_noalloc(const void* q, const void* k_cache, const void* v_cache, void* out,
+                        const int32_t* seq_lens, const int32_t* block_table,
+                        int64_t batch_size, int64_t num_heads, int64_t num_heads_k,
+                        int64_t headdim, int64_t page_size, int64_t num_pages,
+                        int64_t bt_stride, int64_t max_seqlen, float scale, void* stream);
 
 /* Bytes of workspace pgqa_decode_v1 needs for this shape on the current device
  * (no counterpart in the reference, whose workspace is a hidden static buffer,

@@ -38,6 +38,7 @@ SIGNATURES = {
     "run_kernel": (None, [c_void_p] * 4 + [c_void_p, c_void_p] + [c_int64] * 9),
     "pgqa_decode_v1": (ctypes.c_int, [c_void_p] * 6 + [c_int64] * 8 +
                        [c_float, c_void_p, c_size_t, c_void_p]),
+    "pgqa_decode_noalloc": (ctypes.c_int, [c_void_p] * 6 + [c_int64] * 8 + [c_float, c_void_p]),
     "pgqa_workspace_size": (c_size_t, [c_int64] * 5),
     "pgqa_workspace_init": (ctypes.c_int, [c_void_p, c_size_t, c_void_p]),
     "pgqa_last_status": (ctypes.c_int, []),
@@ -54,7 +55,7 @@ STATUS = {
     0: "PGQA_OK", 1: "PGQA_ERR_NULL_POINTER", 2: "PGQA_ERR_BAD_SHAPE",
     3: "PGQA_ERR_UNSUPPORTED", 4: "PGQA_ERR_MISALIGNED", 5: "PGQA_ERR_WORKSPACE",
     6: "PGQA_ERR_CUDA", 7: "PGQA_ERR_NO_DEVICE", 8: "PGQA_ERR_DEVICE_TIMEOUT",
-    9: "PGQA_ERR_DEVICE_BAD_PAGE", 10: "PGQA_ERR_DEVICE_BAD_SEQLEN",
+    9: "PGQA_ERR_DEVICE_BAD_PAGE", 10: "PGQA_ERR_DEVICE_BAD_SEQLEN", 11: "PGQA_ERR_SCRATCH_LIMIT",
 }
 
 _lock = threading.Lock()

@@ -1091,6 +1091,8 @@ extern "C" const char* pgqa_status_string(int status) {
         case PGQA_ERR_DEVICE_TIMEOUT: return "device-side wait timed out";
         case PGQA_ERR_DEVICE_BAD_PAGE: return "block_table entry outside [0, num_pages)";
         case PGQA_ERR_DEVICE_BAD_SEQLEN: return "seq_len outside [0, table capacity]";
+        case PGQA_ERR_SCRATCH_LIMIT:
+            return "shape needs more scratch than the fixed 4 MiB allocation-free buffer";
         default: return "unknown status";
     }
 }
@@ -1172,3 +1174,89 @@ extern "C" int64_t pgqa_simulate_partition(const int32_t* seq_lens, int64_t B, i
 }
 
 extern "C" const char* pgqa_version(void) { return "pgqa-b200 0.1 (sm_100a)"; }
+
+/* ------------------------------------------------------------------------------------ */
+/* Allocation-free entry point                                                          */
+/* ------------------------------------------------------------------------------------ */
+
+/* Scratch for pgqa_decode_noalloc: the same layout pgqa_decode_v1 expects of a caller's
+ * workspace (error word, split records, arrival counters), held in a fixed array that
+ * every GPU loading this library keeps until the process exits.  4 MiB covers the
+ * records of a 148-SM B200 plus arrival counters for about 740,000 (sequence, KV head,
+ * head group) units. */
+constexpr size_t kNoAllocScratchBytes = (size_t)4 << 20;
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace {
+struct NoAllocScratch {
+    bool init = false;
+    int status = PGQA_OK;
+    void* ptr = nullptr;  // device address of g_noalloc_scratch on this device
+};
+NoAllocScratch g_noalloc[pgqa::kMaxDevices];
+std::mutex g_noalloc_mu;
+
+/* Host code may not use g_noalloc_scratch itself (that name is a host-side stand-in,
+ * not a device address): resolve the device address once per device, with that device
+ * current. */
+int noalloc_scratch(int dev, void** out) {
+    if (dev < 0 || dev >= pgqa::kMaxDevices) return PGQA_ERR_NO_DEVICE;
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    NoAllocScratch& s = g_noalloc[dev];
+    if (!s.init) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess || p == nullptr) {
+            cudaGetLastError();
+            s.status = PGQA_ERR_CUDA;
+        } else {
+            s.ptr = p;
+            s.status = PGQA_OK;
+        }
+        s.init = true;
+    }
+    *out = s.ptr;
+    return s.status;
+}
+}  // namespace
+
+extern "C" int pgqa_decode_noalloc(const void* q, const void* k_cache, const void* v_cache,
+                                   void* out, const int32_t* seq_lens,
+                                   const int32_t* block_table, int64_t batch_size,
+                                   int64_t num_heads, int64_t num_heads_k, int64_t headdim,
+                                   int64_t page_size, int64_t num_pages, int64_t bt_stride,
+                                   int64_t max_seqlen, float scale, void* stream) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        cudaGetLastError();
+        return set_status(PGQA_ERR_NO_DEVICE);
+    }
+    DevInfo di;
+    int st = device_info(dev, &di);
+    if (st != PGQA_OK) return set_status(st);
+    pgqa_plan plan;
+    st = make_plan_impl(batch_size, num_heads, num_heads_k, headdim, page_size, di.sms,
+                        di.smem_optin, &plan);
+    if (st != PGQA_OK) return set_status(st);
+    if ((size_t)plan.workspace_bytes > kNoAllocScratchBytes)
+        return set_status(PGQA_ERR_SCRATCH_LIMIT);
+    void* scratch = nullptr;
+    st = noalloc_scratch(dev, &scratch);
+    if (st != PGQA_OK) return set_status(st);
+    // The array keeps the previous call's contents: the error word and the arrival
+    // counters must start at zero (a failed call may have left counters behind).
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    uint8_t* base = static_cast<uint8_t*>(scratch);
+    const size_t counters_off = 256 + records_bytes(plan.grid_ctas);
+    const size_t counters_len = (size_t)plan.workspace_bytes - counters_off;
+    if (cudaMemsetAsync(base, 0, 256, s) != cudaSuccess ||
+        cudaMemsetAsync(base + counters_off, 0, counters_len, s) != cudaSuccess) {
+        cudaGetLastError();
+        return set_status(PGQA_ERR_CUDA);
+    }
+    return set_status(decode_impl(q, k_cache, v_cache, out, seq_lens, block_table, batch_size,
+                                  num_heads, num_heads_k, headdim, page_size, num_pages,
+                                  bt_stride, max_seqlen, scale, scratch, kNoAllocScratchBytes,
+                                  s));
+}
+
