@@ -39,6 +39,7 @@
 #include <string.h>
 
 #include <math.h>
+#include <stddef.h>
 #include <mutex>
 
 #include "../../include/pgqa.h"
@@ -53,7 +54,6 @@ namespace pgqa {
 
 constexpr int kStageBytes = 8192;          // K (2 x 2 KB halves) + V (2 x 2 KB halves)
 constexpr int kHalfBytes = 2048;           // 16 tokens x 64 dims x bf16
-constexpr int kStashRow = 132;             // padded fp32 row (bank-conflict free stores)
 constexpr uint64_t kWaitLimitNs = 1000000000ull;  // 1 s bound on any single wait
 
 enum DeviceErr : int32_t { kErrTimeout = 1, kErrBadPage = 2, kErrBadSeqlen = 4 };
@@ -63,9 +63,9 @@ struct DecodeParams {
     __nv_bfloat16* out;
     const int32_t* seq_lens;
     const int32_t* block_table;
-    float* rec_o;        // [2 * grid][8][128]
-    float* rec_lse;      // [2 * grid][8]
-    int32_t* counters;   // [B * U]
+    float* rec_o;        // [2 * grid][8 M tiles][32 lanes] float4 (O^T fragments)
+    float* rec_lse;      // [2 * grid][8 M tiles][8 heads]
+    int32_t* counters;   // [B * U][8 M tiles] arrival counters
     int32_t* err;        // device error word
     int32_t B, Hq, Hkv, g, n_hg, U;
     int32_t page_size, bt_stride, num_pages;
@@ -76,11 +76,13 @@ struct DecodeParams {
     uint64_t wait_limit_ns;  // bound on every mbarrier wait
 };
 
-/* Per-warp record of a unit cut by a slice boundary (shared memory, after streaming). */
+/* Per-warp record of a unit cut by a slice boundary (shared memory, after streaming),
+ * kept in the MMA accumulator layout: o[mt][lane] holds that lane's four O^T values of
+ * M tile mt, (d, hA) (d, hB) (d+8, hA) (d+8, hB) with d = 16 mt + lane/4,
+ * hA = 2 (lane%4), hB = hA + 1.  Global records use the same layout. */
 struct __align__(16) Stash {
-    float o[8][kStashRow];  // normalised o[h][d]
-    float lse[8];           // log2-sum-exp per head
-    int32_t b, j, valid, pad;
+    float4 o[8][32];  // normalised O^T fragments
+    float lse[8];     // log2-sum-exp per head
 };
 
 struct Cursor {
@@ -130,32 +132,51 @@ __device__ __forceinline__ int64_t unit_begin(const DecodeParams& p, const uint3
     return (int64_t)pre[b] * p.U + (int64_t)j * (pre[b + 1] - pre[b]);
 }
 
-/* Merge `cnt` stashes (LSE merge) for head h, dims [d0, d0+4); result in acc / lse. */
-struct MergeAcc {
-    float m, den;
-    float a[4];
-    __device__ __forceinline__ void init() {
-        m = -INFINITY; den = 0.f; a[0] = a[1] = a[2] = a[3] = 0.f;
+/* Writes M tile mt of an O^T fragment as bf16 output rows: movmatrix turns the lane's
+ * (d, head pair) values into (head = lane/4, d pair) so each lane stores 2 x 32 bits of
+ * the row of head lane/4 (`head_row`).  Collective over the warp; only lanes with
+ * `valid` store. */
+__device__ __forceinline__ void store_out_tile(__nv_bfloat16* head_row, float f0, float f1, float f2,
+                                               float f3, float sA, float sB, int mt, int tig,
+                                               bool valid) {
+    const uint32_t y0 = ptx::movmatrix_t(ptx::pack_bf16x2(f0 * sA, f1 * sB));
+    const uint32_t y1 = ptx::movmatrix_t(ptx::pack_bf16x2(f2 * sA, f3 * sB));
+    if (valid) {
+        *reinterpret_cast<uint32_t*>(head_row + mt * 16 + 2 * tig) = y0;
+        *reinterpret_cast<uint32_t*>(head_row + mt * 16 + 8 + 2 * tig) = y1;
     }
-    __device__ __forceinline__ void add(float lse, float4 o) {
-        if (lse > m) {
-            const float s = ptx::ex2(m - lse);  // 0 when m == -inf
-            den *= s; a[0] *= s; a[1] *= s; a[2] *= s; a[3] *= s;
-            m = lse;
+}
+
+/* Log-sum-exp merge of one head pair of a fragment tile.  Contributions arrive in
+ * batches: each batch's maximum is taken first, so the weights of a batch are
+ * independent exponentials (no serial rescale chain per contribution). */
+struct PairMerge {
+    float mA, mB, dA, dB;
+    float a0, a1, a2, a3;
+    __device__ __forceinline__ void init() {
+        mA = mB = -INFINITY;
+        dA = dB = 0.f;
+        a0 = a1 = a2 = a3 = 0.f;
+    }
+    /* Raise the running maxima to (bA, bB), rescaling what was accumulated. */
+    __device__ __forceinline__ void rebase(float bA, float bB) {
+        if (bA > mA) {
+            const float s = ptx::ex2(mA - bA);
+            dA *= s; a0 *= s; a2 *= s; mA = bA;
         }
-        const float w = ptx::ex2(lse - m);
-        den += w;
-        a[0] = fmaf(w, o.x, a[0]); a[1] = fmaf(w, o.y, a[1]);
-        a[2] = fmaf(w, o.z, a[2]); a[3] = fmaf(w, o.w, a[3]);
+        if (bB > mB) {
+            const float s = ptx::ex2(mB - bB);
+            dB *= s; a1 *= s; a3 *= s; mB = bB;
+        }
+    }
+    /* Add one contribution; its lse must not exceed the current maxima. */
+    __device__ __forceinline__ void add(float lseA, float lseB, float4 v) {
+        const float wA = ptx::ex2(lseA - mA), wB = ptx::ex2(lseB - mB);
+        dA += wA; dB += wB;
+        a0 = fmaf(wA, v.x, a0); a1 = fmaf(wB, v.y, a1);
+        a2 = fmaf(wA, v.z, a2); a3 = fmaf(wB, v.w, a3);
     }
 };
-
-__device__ __forceinline__ void store_bf16x4(__nv_bfloat16* dst, float x, float y, float z, float w) {
-    uint2 v;
-    v.x = ptx::pack_bf16x2(x, y);
-    v.y = ptx::pack_bf16x2(z, w);
-    *reinterpret_cast<uint2*>(dst) = v;
-}
 
 template <int W, int S>
 __global__ void __launch_bounds__(W * 32, 1)
@@ -167,9 +188,8 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
     uint8_t* smem = smem_raw + ((1024u - (ptx::smem_u32(smem_raw) & 1023u)) & 1023u);
     uint8_t* ring = smem;                                                  // W*S*8 KB
     uint64_t* bars = reinterpret_cast<uint64_t*>(ring + W * S * kStageBytes);  // W*S
-    int32_t* misc = reinterpret_cast<int32_t*>(bars + W * S);               // 32 ints
-    uint32_t* pre = reinterpret_cast<uint32_t*>(misc + 32);                 // B+1
-    Stash* stash = reinterpret_cast<Stash*>(ring);                          // reuses the ring
+    int32_t* misc = reinterpret_cast<int32_t*>(bars + W * S);               // 64 ints
+    uint32_t* pre = reinterpret_cast<uint32_t*>(misc + 64);                 // B+1
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
@@ -182,10 +202,7 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
         ptx::prefetch_tensormap(&vmap);
         for (int i = 0; i < W * S; ++i) ptx::mbar_init(ptx::smem_u32(bars + i), 1);
         ptx::fence_mbar_init();
-        misc[16] = -1;  // global-merge flags: unit b of record slot 0 / 1
-        misc[17] = -1;
-        misc[18] = -1;  // unit j of record slot 0 / 1
-        misc[19] = -1;
+    
     }
 
     /* ---- chunk prefix over sequences (every CTA computes it; B is small) ---- */
@@ -454,14 +471,9 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
                     __nv_bfloat16* orow =
                         p.out + ((int64_t)cc.b * p.Hq + kvh * p.g + hg * kHeadsPerGroup + gid) * kHeadDim;
 #pragma unroll
-                    for (int mt = 0; mt < 8; ++mt) {
-                        const uint32_t y0 = ptx::movmatrix_t(ptx::pack_bf16x2(o[mt][0] * invA, o[mt][1] * invB));
-                        const uint32_t y1 = ptx::movmatrix_t(ptx::pack_bf16x2(o[mt][2] * invA, o[mt][3] * invB));
-                        if (gid < nh_valid) {
-                            *reinterpret_cast<uint32_t*>(orow + mt * 16 + 2 * tig) = y0;
-                            *reinterpret_cast<uint32_t*>(orow + mt * 16 + 8 + 2 * tig) = y1;
-                        }
-                    }
+                    for (int mt = 0; mt < 8; ++mt)
+                        store_out_tile(orow, o[mt][0], o[mt][1], o[mt][2], o[mt][3], invA, invB, mt,
+                                       tig, gid < nh_valid);
                 } else {
                     const float lseA = m2[0] + ptx::lg2(lA);
                     const float lseB = m2[1] + ptx::lg2(lB);
@@ -498,169 +510,147 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
         }
     }
 
-    /* ---- CTA level: stash cut units, merge across warps ---- */
-    __syncthreads();  // every warp has finished with its ring; reuse it for stashes
-    if (warp < W) {
-        Stash& s0 = stash[warp * 2 + 0];
-        Stash& s1 = stash[warp * 2 + 1];
+    /* ---- park this warp's cut units in its own (now idle) ring: no TMA is in flight ----
+     * Parked state f = 2 * warp + slot lives at the start of warp `warp`'s ring; its key
+     * (b, j), or (-1, -1) when empty, goes to a compact table for the run scan. */
+    auto stash_addr = [&](int f) -> uint32_t {
+        return ring_base + (uint32_t)((f >> 1) * S * kStageBytes) + (uint32_t)((f & 1) * sizeof(Stash));
+    };
+    const uint32_t keys_base = ptx::smem_u32(misc + 32);  // int2 keys[2W], W <= 16
+    {
         const bool v0 = (warp < wa) && have_first && !aborted;
         const bool v1 = (warp < wa) && have_last && !aborted;
+        const uint32_t a0 = stash_addr(2 * warp), a1 = stash_addr(2 * warp + 1);
         if (v0) {
 #pragma unroll
-            for (int mt = 0; mt < 8; ++mt) {
-                s0.o[2 * tig][mt * 16 + gid] = fo[mt][0];
-                s0.o[2 * tig + 1][mt * 16 + gid] = fo[mt][1];
-                s0.o[2 * tig][mt * 16 + gid + 8] = fo[mt][2];
-                s0.o[2 * tig + 1][mt * 16 + gid + 8] = fo[mt][3];
-            }
-            if (gid == 0) { s0.lse[2 * tig] = flse[0]; s0.lse[2 * tig + 1] = flse[1]; }
+            for (int mt = 0; mt < 8; ++mt)
+                ptx::sts_f4(a0 + (mt * 32 + lane) * 16, make_float4(fo[mt][0], fo[mt][1], fo[mt][2], fo[mt][3]));
+            if (gid == 0) ptx::sts_f2(a0 + offsetof(Stash, lse) + tig * 8, make_float2(flse[0], flse[1]));
         }
         if (v1) {
 #pragma unroll
-            for (int mt = 0; mt < 8; ++mt) {
-                s1.o[2 * tig][mt * 16 + gid] = o[mt][0];
-                s1.o[2 * tig + 1][mt * 16 + gid] = o[mt][1];
-                s1.o[2 * tig][mt * 16 + gid + 8] = o[mt][2];
-                s1.o[2 * tig + 1][mt * 16 + gid + 8] = o[mt][3];
-            }
-            if (gid == 0) { s1.lse[2 * tig] = m2[0]; s1.lse[2 * tig + 1] = m2[1]; }
+            for (int mt = 0; mt < 8; ++mt)
+                ptx::sts_f4(a1 + (mt * 32 + lane) * 16, make_float4(o[mt][0], o[mt][1], o[mt][2], o[mt][3]));
+            if (gid == 0) ptx::sts_f2(a1 + offsetof(Stash, lse) + tig * 8, make_float2(m2[0], m2[1]));
         }
         if (lane == 0) {
-            s0.valid = v0; s0.b = first_u.b; s0.j = first_u.j;
-            s1.valid = v1; s1.b = last_u.b; s1.j = last_u.j;
+            ptx::sts_i2(keys_base + (2 * warp) * 8, v0 ? make_int2(first_u.b, first_u.j) : make_int2(-1, -1));
+            ptx::sts_i2(keys_base + (2 * warp + 1) * 8, v1 ? make_int2(last_u.b, last_u.j) : make_int2(-1, -1));
         }
     }
     __syncthreads();
 
-    if (warp < wa) {
-        const int d0 = lane * 4;
-#pragma unroll 1
-        for (int sidx = 0; sidx < 2; ++sidx) {
-            const Stash& me = stash[warp * 2 + sidx];
-            if (!me.valid) continue;
-            const int32_t ub = me.b, uj = me.j;
-            // Is this warp the last contributor inside the CTA?
-            if (warp + 1 < wa) {
-                const Stash& nx = stash[(warp + 1) * 2];
-                if (nx.valid && nx.b == ub && nx.j == uj) continue;
-            }
-            MergeAcc acc[8];
-#pragma unroll
-            for (int h = 0; h < 8; ++h) acc[h].init();
-#pragma unroll
-            for (int h = 0; h < 8; ++h)
-                acc[h].add(me.lse[h], *reinterpret_cast<const float4*>(&me.o[h][d0]));
-            if (sidx == 0) {
-                // u is this warp's first unit: earlier warps of the CTA may hold its head.
-                for (int k = warp - 1; k >= 0; --k) {
-                    const Stash& c1 = stash[k * 2 + 1];
-                    const Stash& c0 = stash[k * 2 + 0];
-                    const bool in1 = c1.valid && c1.b == ub && c1.j == uj;
-                    const bool in0 = c0.valid && c0.b == ub && c0.j == uj;
-                    const Stash* st = in1 ? &c1 : (in0 ? &c0 : nullptr);
-                    if (st == nullptr) break;
-#pragma unroll
-                    for (int h = 0; h < 8; ++h)
-                        acc[h].add(st->lse[h], *reinterpret_cast<const float4*>(&st->o[h][d0]));
-                    if (in1) break;  // u began inside warp k
-                }
-            }
-            const int32_t n_u = (int32_t)(pre[ub + 1] - pre[ub]);
-            const int64_t ubeg = unit_begin(p, pre, ub, uj);
-            const int32_t kvh = uj / p.n_hg;
-            const int32_t hg = uj - kvh * p.n_hg;
-            const int nhv = min(kHeadsPerGroup, p.g - hg * kHeadsPerGroup);
-            if (ubeg >= cs && ubeg + n_u <= ce) {
-                // Unit lies inside this CTA: final output.
-                __nv_bfloat16* orow = p.out + ((int64_t)ub * p.Hq + kvh * p.g + hg * kHeadsPerGroup) * kHeadDim;
-                for (int h = 0; h < nhv; ++h) {
-                    const float inv = 1.f / acc[h].den;
-                    store_bf16x4(orow + h * kHeadDim + d0, acc[h].a[0] * inv, acc[h].a[1] * inv,
-                                 acc[h].a[2] * inv, acc[h].a[3] * inv);
-                }
-            } else {
-                // Unit crosses the CTA boundary: write this CTA's record, count arrivals.
-                const int64_t slot = record_slot(blockIdx.x, cs, ubeg);
-                float* ro = p.rec_o + slot * (8 * kHeadDim);
-#pragma unroll
-                for (int h = 0; h < 8; ++h) {
-                    const float inv = 1.f / acc[h].den;
-                    *reinterpret_cast<float4*>(ro + h * kHeadDim + d0) =
-                        make_float4(acc[h].a[0] * inv, acc[h].a[1] * inv, acc[h].a[2] * inv,
-                                    acc[h].a[3] * inv);
-                }
-                if (lane < 8) {
-                    float lse = 0.f;
-#pragma unroll
-                    for (int h = 0; h < 8; ++h)
-                        if (h == lane) lse = acc[h].m + ptx::lg2(acc[h].den);
-                    p.rec_lse[slot * 8 + lane] = lse;
-                }
-                __syncwarp();  // the warp's record stores happen before lane 0's release
-                if (lane == 0) {
-                    const int64_t c_first = slice_owner(ubeg, nct, T);
-                    const int64_t c_last = slice_owner(ubeg + n_u - 1, nct, T);
-                    const int32_t need = (int32_t)(c_last - c_first + 1);
-                    int32_t* cnt = p.counters + (int64_t)ub * p.U + uj;
-                    ptx::fence_acq_rel_gpu();  // release this CTA's record
-                    const int32_t prev = ptx::atom_add_relaxed_gpu(cnt, 1);
-                    if (prev == need - 1) {
-                        ptx::fence_acq_rel_gpu();  // acquire the other CTAs' records
-                        *cnt = 0;  // leave the workspace zeroed for the next call
-                        const int fs = (slot & 1) ? 1 : 0;
-                        misc[16 + fs] = ub;
-                        misc[18 + fs] = uj;
-                    }
-                }
-            }
-        }
-    }
-    __syncthreads();
+    /* ---- CTA level: merge every cut unit; warp w owns M tiles w, w+W, ... ----
+     * Parked states of one unit form a run in (warp, slot) order (slices are contiguous).
+     * For each run every warp LSE-merges its M tiles across the run, then either stores
+     * the output (unit inside this CTA) or writes that tile of the CTA's record and
+     * counts arrivals per (unit, M tile); the warp that completes a tile merges it across
+     * all CTAs' records.  Merges take the maximum first and select, never branch, on
+     * membership, so every load of a pass is issued at once. */
+    constexpr int NF = 2 * W;
+    int2 key = make_int2(-1, -1);
+    if (lane < NF) key = ptx::lds_i2(keys_base + lane * 8);
+    const unsigned vmask = __ballot_sync(0xffffffffu, lane < NF && key.x >= 0);
+    unsigned rem = vmask;
+    while (rem) {
+        const int fa = __ffs(rem) - 1;
+        const int32_t ub = __shfl_sync(0xffffffffu, key.x, fa);
+        const int32_t uj = __shfl_sync(0xffffffffu, key.y, fa);
+        const unsigned run = __ballot_sync(0xffffffffu, ((vmask >> lane) & 1u) && key.x == ub && key.y == uj);
+        rem &= ~run;
 
-    /* ---- global merge of units whose last record this CTA wrote ----
-     * One pass per (head, 4 dims) per thread: the lse and o of up to 8 records are
-     * loaded together (one L2 round trip), then folded with a running max. */
-#pragma unroll 1
-    for (int fs = 0; fs < 2; ++fs) {
-        const int32_t ub = misc[16 + fs];
-        if (ub < 0) continue;  // same value in every thread of the CTA
-        const int32_t uj = misc[18 + fs];
         const int32_t n_u = (int32_t)(pre[ub + 1] - pre[ub]);
         const int64_t ubeg = unit_begin(p, pre, ub, uj);
-        const int64_t c_first = slice_owner(ubeg, nct, T);
-        const int64_t c_last = slice_owner(ubeg + n_u - 1, nct, T);
-        const int nrec = (int)(c_last - c_first + 1);
         const int32_t kvh = uj / p.n_hg;
         const int32_t hg = uj - kvh * p.n_hg;
         const int nhv = min(kHeadsPerGroup, p.g - hg * kHeadsPerGroup);
-        for (int idx = tid; idx < 8 * 32; idx += NT) {
-            const int h = idx >> 5;
-            const int d0 = (idx & 31) * 4;
-            MergeAcc acc;
-            acc.init();
-            for (int r0 = 0; r0 < nrec; r0 += 8) {
-                float lse[8];
-                float4 v[8];
+        const bool inside = (ubeg >= cs && ubeg + n_u <= ce);
+        __nv_bfloat16* orow =
+            p.out + ((int64_t)ub * p.Hq + kvh * p.g + hg * kHeadsPerGroup + gid) * kHeadDim;
+        for (int mt = warp; mt < 8; mt += W) {
+            float2 ls[NF];
+            float4 v[NF];
 #pragma unroll
-                for (int u = 0; u < 8; ++u) {
+            for (int f = 0; f < NF; ++f) {
+                ls[f] = ptx::lds_f2(stash_addr(f) + offsetof(Stash, lse) + tig * 8);
+                v[f] = ptx::lds_f4(stash_addr(f) + (mt * 32 + lane) * 16);
+            }
+            float bA = -INFINITY, bB = -INFINITY;
+#pragma unroll
+            for (int f = 0; f < NF; ++f) {
+                const bool in = (run >> f) & 1u;
+                bA = in ? fmaxf(bA, ls[f].x) : bA;
+                bB = in ? fmaxf(bB, ls[f].y) : bB;
+            }
+            float dA = 0.f, dB = 0.f, a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll
+            for (int f = 0; f < NF; ++f) {
+                const bool in = (run >> f) & 1u;
+                const float wA = ptx::ex2(ls[f].x - bA), wB = ptx::ex2(ls[f].y - bB);
+                dA = in ? dA + wA : dA;
+                dB = in ? dB + wB : dB;
+                a0 = in ? fmaf(wA, v[f].x, a0) : a0;
+                a1 = in ? fmaf(wB, v[f].y, a1) : a1;
+                a2 = in ? fmaf(wA, v[f].z, a2) : a2;
+                a3 = in ? fmaf(wB, v[f].w, a3) : a3;
+            }
+            const float invA = 1.f / dA, invB = 1.f / dB;
+            if (inside) {
+                store_out_tile(orow, a0, a1, a2, a3, invA, invB, mt, tig, gid < nhv);
+                continue;
+            }
+            const int64_t slot = record_slot(blockIdx.x, cs, ubeg);
+            reinterpret_cast<float4*>(p.rec_o)[(slot * 8 + mt) * 32 + lane] =
+                make_float4(a0 * invA, a1 * invB, a2 * invA, a3 * invB);
+            if (gid == 0)
+                reinterpret_cast<float2*>(p.rec_lse)[(slot * 8 + mt) * 4 + tig] =
+                    make_float2(bA + ptx::lg2(dA), bB + ptx::lg2(dB));
+            const int64_t c_first = slice_owner(ubeg, nct, T);
+            const int64_t c_last = slice_owner(ubeg + n_u - 1, nct, T);
+            int last = 0;
+            __syncwarp();  // the warp's record stores happen before lane 0's release
+            if (lane == 0) {
+                int32_t* cnt = p.counters + ((int64_t)ub * p.U + uj) * 8 + mt;
+                ptx::fence_acq_rel_gpu();  // release this CTA's record tile
+                const int32_t prev = ptx::atom_add_relaxed_gpu(cnt, 1);
+                if (prev == (int32_t)(c_last - c_first)) {
+                    ptx::fence_acq_rel_gpu();  // acquire the other CTAs' tiles
+                    *cnt = 0;                  // leave the workspace zeroed for the next call
+                    last = 1;
+                }
+            }
+            last = __shfl_sync(0xffffffffu, last, 0);
+            __syncwarp();
+            if (!last) continue;
+            // This warp completed tile mt: merge it over every CTA's record, 16 at a time.
+            const int nrec = (int)(c_last - c_first + 1);
+            // Record slots: CTA c_first holds the unit's head in slot 2c+1 unless its slice
+            // starts exactly at the unit; every later CTA holds it in slot 2c.
+            const int64_t slot0 = record_slot(c_first, slice_begin(c_first, nct, T), ubeg);
+            PairMerge g;
+            g.init();
+            for (int r0 = 0; r0 < nrec; r0 += 16) {
+                float2 lse[16];
+                float4 rv[16];
+#pragma unroll
+                for (int u = 0; u < 16; ++u) {
+                    lse[u] = make_float2(-INFINITY, -INFINITY);
+                    rv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
                     if (r0 + u < nrec) {
-                        const int64_t c = c_first + r0 + u;
-                        const int64_t slot = record_slot(c, slice_begin(c, nct, T), ubeg);
-                        lse[u] = __ldcg(p.rec_lse + slot * 8 + h);
-                        v[u] = __ldcg(reinterpret_cast<const float4*>(
-                            p.rec_o + slot * (8 * kHeadDim) + h * kHeadDim + d0));
+                        const int64_t sl = (r0 + u == 0) ? slot0 : 2 * (c_first + r0 + u);
+                        lse[u] = __ldcg(reinterpret_cast<const float2*>(p.rec_lse) + (sl * 8 + mt) * 4 + tig);
+                        rv[u] = __ldcg(reinterpret_cast<const float4*>(p.rec_o) + (sl * 8 + mt) * 32 + lane);
                     }
                 }
+                float rA = -INFINITY, rB = -INFINITY;
 #pragma unroll
-                for (int u = 0; u < 8; ++u)
-                    if (r0 + u < nrec) acc.add(lse[u], v[u]);
+                for (int u = 0; u < 16; ++u) { rA = fmaxf(rA, lse[u].x); rB = fmaxf(rB, lse[u].y); }
+                g.rebase(rA, rB);
+#pragma unroll
+                for (int u = 0; u < 16; ++u)
+                    if (r0 + u < nrec) g.add(lse[u].x, lse[u].y, rv[u]);
             }
-            if (h < nhv) {
-                const float inv = 1.f / acc.den;
-                __nv_bfloat16* orow =
-                    p.out + ((int64_t)ub * p.Hq + kvh * p.g + hg * kHeadsPerGroup + h) * kHeadDim + d0;
-                store_bf16x4(orow, acc.a[0] * inv, acc.a[1] * inv, acc.a[2] * inv, acc.a[3] * inv);
-            }
+            store_out_tile(orow, g.a0, g.a1, g.a2, g.a3, 1.f / g.dA, 1.f / g.dB, mt, tig, gid < nhv);
         }
     }
 }
@@ -699,8 +689,8 @@ const Knobs& knobs() {
 }
 
 constexpr int kDefaultWarps = 8;
-constexpr int kDefaultStages = 3;
-constexpr int kDefaultMinChunks = 4;
+constexpr int kDefaultStages = 2;
+constexpr int kDefaultMinChunks = 2;
 constexpr int kB200Sms = 148;
 constexpr int kB200SmemOptin = 232448;
 
@@ -710,7 +700,7 @@ int smem_bytes_for(int warps, int stages, int64_t B) {
     size_t s = 1024;  // alignment slack for the 1024-byte aligned ring
     s += (size_t)warps * stages * kStageBytes;
     s += (size_t)warps * stages * 8;
-    s += 32 * 4;
+    s += 64 * 4;
     s += align_up((size_t)(B + 1) * 4, 16);
     // The stash area reuses the ring; it must fit.
     const size_t stash = (size_t)warps * 2 * sizeof(Stash);
@@ -734,15 +724,16 @@ int validate_shape(int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int64_t P) {
 /* Workspace layout: [error word | record lse | record o | arrival counters].  The record
  * regions depend only on the grid, so the counters start at the same offset for every
  * shape: a workspace reused across shapes never reads old records as counters. */
+size_t record_lse_bytes(int grid) { return align_up((size_t)2 * grid * 8 * 8 * 4, 256); }
+
 size_t records_bytes(int grid) {
-    return align_up((size_t)2 * grid * 8 * 4, 256) +
-           align_up((size_t)2 * grid * 8 * kHeadDim * 4, 256);
+    return record_lse_bytes(grid) + align_up((size_t)2 * grid * 8 * kHeadDim * 4, 256);
 }
 
 int64_t workspace_bytes_for(int64_t B, int64_t U, int grid) {
     size_t s = 256;                                   // error word (+ pad)
     s += records_bytes(grid);                         // record lse + record o
-    s += align_up((size_t)B * U * 4, 256);            // arrival counters
+    s += align_up((size_t)B * U * 8 * 4, 256);        // arrival counters per M tile
     return (int64_t)s;
 }
 
@@ -967,7 +958,7 @@ int decode_impl(const void* q, const void* k, const void* v, void* out, const in
     p.err = reinterpret_cast<int32_t*>(ws);
     size_t off = 256;
     p.rec_lse = reinterpret_cast<float*>(ws + off);
-    off += align_up((size_t)2 * plan.grid_ctas * 8 * 4, 256);
+    off += record_lse_bytes(plan.grid_ctas);
     p.rec_o = reinterpret_cast<float*>(ws + off);
     off = 256 + records_bytes(plan.grid_ctas);
     p.counters = reinterpret_cast<int32_t*>(ws + off);
@@ -1182,7 +1173,7 @@ extern "C" const char* pgqa_version(void) { return "pgqa-b200 0.1 (sm_100a)"; }
 /* Scratch for pgqa_decode_noalloc: the same layout pgqa_decode_v1 expects of a caller's
  * workspace (error word, split records, arrival counters), held in a fixed array that
  * every GPU loading this library keeps until the process exits.  4 MiB covers the
- * records of a 148-SM B200 plus arrival counters for about 740,000 (sequence, KV head,
+ * records of a 148-SM B200 plus arrival counters for about 90,000 (sequence, KV head,
  * head group) units. */
 constexpr size_t kNoAllocScratchBytes = (size_t)4 << 20;
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];

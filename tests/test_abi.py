@@ -55,7 +55,7 @@ def test_plan_for_benchmark_shapes(shape):
     assert st == 0 and plan.status == 0
     assert plan.grid_ctas == 148
     assert plan.smem_bytes <= 232448
-    assert plan.stages >= 3
+    assert plan.stages >= 2
     assert plan.head_groups == -(-(Hq // Hkv) // 8)
     assert plan.workspace_bytes > 0
 
@@ -69,10 +69,12 @@ def test_plan_rejects_bad_shapes():
     assert st == 0 and plan.grid_ctas == 132
 
 
-def test_plan_shrinks_ring_for_large_batches():
-    _, small = make_plan(8, 32, 8, 128, 16)
-    _, big = make_plan(20000, 32, 8, 128, 16)
-    assert big.status == 0 and big.stages < small.stages and big.smem_bytes <= 232448
+def test_plan_limits_batch_by_prefix_table():
+    # the per-sequence chunk prefix lives in shared memory next to the TMA rings
+    _, ok = make_plan(20000, 32, 8, 128, 16)
+    assert ok.status == 0 and ok.smem_bytes <= 232448
+    st, _ = make_plan(40000, 32, 8, 128, 16)
+    assert st == 3
 
 
 FAKE = ctypes.c_void_p(0x10000)
