@@ -52,6 +52,8 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-host-budget-gb", type=float, default=8.0)
     ap.add_argument("--out", default=None, help="also append the JSON line to this file")
+    ap.add_argument("--profile", type=int, default=0,
+                    help="run N decode calls of the workload and exit (for ncu captures)")
     return ap.parse_args()
 
 
@@ -234,6 +236,10 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.profile:
+        profile_calls(args, world)
+        return
 
     if args.impl == "reference":
         if world > 1:
@@ -440,6 +446,24 @@ def main():
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def profile_calls(args, world):
+    """N back-to-back decode calls of the workload on cuda:0, no timing (ncu driver)."""
+    import torch
+    from mx_flash_attn_kernel_opt__b200 import inputs, ops
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    name = workload_for(args, world)
+    inp = inputs.baseline_config(name, device=dev)
+    out = torch.empty_like(inp.q)
+    ws = ops.workspace_for(inp.batch, inp.num_heads, inp.num_heads_k, 128, inp.page_size, dev)
+    for _ in range(args.profile):
+        ops.decode(inp.q, inp.k, inp.v, inp.block_table, inp.seq_lens, scale=inp.scale, out=out,
+                   workspace=ws)
+    torch.cuda.synchronize(dev)
+    ops.check_device_error(ws, dev)
+    print(json.dumps({"profile_calls": args.profile, "workload": name}))
 
 
 def e2e_measure(inp, dev, stream, steps, budget_gb, world):
