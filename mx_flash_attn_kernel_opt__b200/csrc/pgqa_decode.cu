@@ -202,8 +202,10 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
         ptx::prefetch_tensormap(&vmap);
         for (int i = 0; i < W * S; ++i) ptx::mbar_init(ptx::smem_u32(bars + i), 1);
         ptx::fence_mbar_init();
-    
     }
+    // Launched as a programmatic dependent: everything above overlaps the previous
+    // kernel's tail; no global memory is touched before the previous grid is complete.
+    ptx::griddep_wait();
 
     /* ---- chunk prefix over sequences (every CTA computes it; B is small) ---- */
     {
@@ -510,6 +512,10 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
         }
     }
 
+    // Streaming is over: let the next kernel in the stream start launching (it still
+    // waits for this grid's completion before it reads any memory).
+    ptx::griddep_launch_dependents();
+
     /* ---- park this warp's cut units in its own (now idle) ring: no TMA is in flight ----
      * Parked state f = 2 * warp + slot lives at the start of warp `warp`'s ring; its key
      * (b, j), or (-1, -1) when empty, goes to a compact table for the run scan. */
@@ -678,13 +684,15 @@ int env_int(const char* name, int dflt) {
     return atoi(v);
 }
 
-/* Sweep knobs (unset in normal use): PGQA_WARPS, PGQA_STAGES, PGQA_MIN_CHUNKS, PGQA_GRID. */
+/* Sweep knobs (unset in normal use): PGQA_WARPS, PGQA_STAGES, PGQA_MIN_CHUNKS, PGQA_GRID,
+ * PGQA_NO_PDL (plain launch instead of a programmatic dependent launch). */
 struct Knobs {
-    int warps, stages, min_chunks, grid;
+    int warps, stages, min_chunks, grid, no_pdl;
 };
 const Knobs& knobs() {
     static const Knobs k = {env_int("PGQA_WARPS", 0), env_int("PGQA_STAGES", 0),
-                            env_int("PGQA_MIN_CHUNKS", 0), env_int("PGQA_GRID", 0)};
+                            env_int("PGQA_MIN_CHUNKS", 0), env_int("PGQA_GRID", 0),
+                            env_int("PGQA_NO_PDL", 0)};
     return k;
 }
 
@@ -891,9 +899,22 @@ int launch_variant(const CUtensorMap& km, const CUtensorMap& vm, const DecodePar
         }
         configured_smem[dev] = smem;
     }
-    kern<<<grid, W * 32, smem, stream>>>(km, vm, p);
-    const cudaError_t e = cudaGetLastError();
-    return e == cudaSuccess ? PGQA_OK : PGQA_ERR_CUDA;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(W * 32);
+    cfg.dynamicSmemBytes = (size_t)smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = knobs().no_pdl ? 0 : 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, km, vm, p);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return PGQA_ERR_CUDA;
+    }
+    return PGQA_OK;
 }
 
 int launch(const pgqa_plan& plan, const CUtensorMap& km, const CUtensorMap& vm,

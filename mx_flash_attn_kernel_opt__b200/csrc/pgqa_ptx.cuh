@@ -121,6 +121,13 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t&
                  : "r"(addr));
 }
 
+/* Programmatic dependent launch: wait until every grid this one depends on has
+ * completed and its memory is visible; allow dependents to start launching. */
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 /* Explicit shared-memory accesses by 32-bit shared-window address. */
 __device__ __forceinline__ float4 lds_f4(uint32_t addr) {
     float4 v;
