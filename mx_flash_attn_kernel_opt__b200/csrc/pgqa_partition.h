@@ -46,14 +46,22 @@ PGQA_HD int64_t seq_chunks(int64_t len, int64_t cap_tokens) {
     return ceil_div64(len, kChunkTokens);
 }
 
+/* Products below this bound fit 32-bit unsigned arithmetic (much cheaper on the GPU
+ * than 64-bit division); the results are identical either way. */
+constexpr int64_t kSmallProduct = 0xffffffffll;
+
 /* Start of slice i when [0, total) is cut into n equal contiguous slices. */
 PGQA_HD int64_t slice_begin(int64_t i, int64_t n, int64_t total) {
+    if (i * total <= kSmallProduct) return (int64_t)((uint32_t)(i * total) / (uint32_t)n);
     return (i * total) / n;
 }
 
 /* Index of the slice that contains position x (0 <= x < total). */
 PGQA_HD int64_t slice_owner(int64_t x, int64_t n, int64_t total) {
-    return ((x + 1) * n - 1) / total;
+    const int64_t num = (x + 1) * n - 1;
+    if (num <= kSmallProduct && total <= kSmallProduct)
+        return (int64_t)((uint32_t)num / (uint32_t)total);
+    return num / total;
 }
 
 /* Number of active CTAs for `total` chunks: every active warp gets at least
