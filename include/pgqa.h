@@ -10,7 +10,7 @@
  *     out[b,h] = softmax(scale * q[b,h] . K[tokens, kv]^T) . V[tokens, kv]
  *
  * with bf16 inputs/outputs and fp32 accumulation.  Layouts (all contiguous):
- *     q, out        [B, 1, Hq, D]                    bf16
+ *     q, out        [B, Sq, Hq, D]  (Sq = 1 for decode) bf16
  *     k, v pools    [num_pages, page_size, Hkv, D]   bf16
  *     seq_lens      [B]                              int32
  *     block_table   [B, bt_stride]                   int32
@@ -36,7 +36,7 @@ enum pgqa_status {
     PGQA_OK = 0,
     PGQA_ERR_NULL_POINTER = 1,      /* a required pointer is NULL                       */
     PGQA_ERR_BAD_SHAPE = 2,         /* B/Hq/Hkv/D/page_size/num_pages/stride invalid    */
-    PGQA_ERR_UNSUPPORTED = 3,       /* valid but not implemented (D != 128, Sq != 1 ...) */
+    PGQA_ERR_UNSUPPORTED = 3,       /* valid but not implemented (D != 128, P % 16 ...) */
     PGQA_ERR_MISALIGNED = 4,        /* a pointer violates the alignment contract        */
     PGQA_ERR_WORKSPACE = 5,         /* workspace missing / too small / allocation failed */
     PGQA_ERR_CUDA = 6,              /* a CUDA runtime/driver call failed                */
@@ -57,6 +57,9 @@ enum pgqa_status {
  * pgqa_last_status().  The first call on a device allocates the library's
  * per-device workspace (cudaMalloc), so the first call must not be inside a
  * CUDA-graph capture.
+ * Beyond the reference (which fixes seqlen_q = 1, causal = 0; task.md:64-66),
+ * seqlen_q >= 1 query tokens per sequence are accepted, q and output being
+ * (B, seqlen_q, Hq, D); with causal = 1 token i sees keys [0, L - seqlen_q + i].
  */
 void run_kernel(const void* q, const void* k_cache_paged, const void* v_cache_paged,
                 void* output, const int32_t* cache_seqlens, const int32_t* block_table,
@@ -83,6 +86,20 @@ int pgqa_decode_v1(const void* q, const void* k_cache, const void* v_cache, void
                    int64_t num_heads, int64_t num_heads_k, int64_t headdim,
                    int64_t page_size, int64_t num_pages, int64_t bt_stride,
                    int64_t max_seqlen, float scale, void* workspace, size_t workspace_bytes,
+                   void* stream);
+
+/*
+ * pgqa_decode_v1 with seqlen_q query tokens per sequence (no counterpart symbol in the
+ * reference; the ABI run_kernel already carries seqlen_q and causal, task.md:40-53).
+ * q and out are [B, seqlen_q, Hq, D]; query token i of sequence b sees keys
+ * [0, L_b) or, with causal = 1, [0, L_b - seqlen_q + i] (a query with no visible key
+ * gives zeros).  The workspace must hold pgqa_workspace_size_v2(...) bytes.
+ */
+int pgqa_decode_v2(const void* q, const void* k_cache, const void* v_cache, void* out,
+                   const int32_t* seq_lens, const int32_t* block_table, int64_t batch_size,
+                   int64_t seqlen_q, int64_t num_heads, int64_t num_heads_k, int64_t headdim,
+                   int64_t page_size, int64_t num_pages, int64_t bt_stride, int64_t max_seqlen,
+                   int64_t causal, float scale, void* workspace, size_t workspace_bytes,
                    void* stream);
 
 /*
@@ -117,6 +134,11 @@ int pgqa_decode_noalloc(const void* q, const void* k_cache, const void* v_cache,
  * submission_clean.cu:478-491).  Returns 0 on invalid shapes. */
 size_t pgqa_workspace_size(int64_t batch_size, int64_t num_heads, int64_t num_heads_k,
                            int64_t headdim, int64_t page_size);
+
+/* Workspace bytes for pgqa_decode_v2 with seqlen_q query tokens (no counterpart in
+ * the reference).  Returns 0 on invalid shapes. */
+size_t pgqa_workspace_size_v2(int64_t batch_size, int64_t seqlen_q, int64_t num_heads,
+                              int64_t num_heads_k, int64_t headdim, int64_t page_size);
 
 /* Zero a caller-provided workspace on `stream` (asynchronous). */
 int pgqa_workspace_init(void* workspace, size_t workspace_bytes, void* stream);

@@ -68,6 +68,9 @@ struct DecodeParams {
     int32_t* counters;   // [B * U][8 M tiles] arrival counters
     int32_t* err;        // device error word
     int32_t B, Hq, Hkv, g, n_hg, U;
+    int32_t Sq;      // query tokens per sequence
+    int32_t rows;    // query rows per KV head = g * Sq (row r: head r / Sq, token r % Sq)
+    int32_t causal;  // query token i sees keys [0, L - Sq + i] instead of [0, L)
     int32_t page_size, bt_stride, num_pages;
     int64_t cap_tokens;  // bt_stride * page_size (clamp for seq_lens)
     float scale_log2;    // scale * log2(e)
@@ -147,9 +150,28 @@ __device__ __forceinline__ void store_out_tile(__nv_bfloat16* head_row, float f0
     }
 }
 
+/* Query row r (of the Hq/Hkv * Sq rows of KV head kvh) of sequence b: head kvh*g + r/Sq,
+ * token r%Sq.  Returns its offset (in elements) in q / out, whose layout is
+ * [B, Sq, Hq, 128]. */
+template <bool MQ>
+__device__ __forceinline__ int64_t row_offset(const DecodeParams& p, int32_t b, int32_t kvh, int r) {
+    if (!MQ) return ((int64_t)b * p.Hq + kvh * p.g + r) * kHeadDim;  // Sq == 1
+    const int h = r / p.Sq;
+    const int i = r - h * p.Sq;
+    return (((int64_t)b * p.Sq + i) * p.Hq + kvh * p.g + h) * kHeadDim;
+}
+
+/* Keys visible to query row r of a sequence of length L. */
+template <bool MQ>
+__device__ __forceinline__ int32_t row_limit(const DecodeParams& p, int r, int32_t L) {
+    if (!MQ || !p.causal || r >= p.rows) return L;
+    return L - p.Sq + (r - (r / p.Sq) * p.Sq) + 1;
+}
+
 /* Log-sum-exp merge of one head pair of a fragment tile.  Contributions arrive in
  * batches: each batch's maximum is taken first, so the weights of a batch are
  * independent exponentials (no serial rescale chain per contribution). */
+template <bool MQ>
 struct PairMerge {
     float mA, mB, dA, dB;
     float a0, a1, a2, a3;
@@ -169,16 +191,22 @@ struct PairMerge {
             dB *= s; a1 *= s; a3 *= s; mB = bB;
         }
     }
-    /* Add one contribution; its lse must not exceed the current maxima. */
+    /* Add one contribution; its lse must not exceed the current maxima.  A row whose
+     * contributions are all empty (lse = -inf; only with several query tokens) keeps
+     * weight 0. */
     __device__ __forceinline__ void add(float lseA, float lseB, float4 v) {
-        const float wA = ptx::ex2(lseA - mA), wB = ptx::ex2(lseB - mB);
+        const float wA = ptx::ex2(lseA - ((MQ && mA == -INFINITY) ? 0.f : mA));
+        const float wB = ptx::ex2(lseB - ((MQ && mB == -INFINITY) ? 0.f : mB));
         dA += wA; dB += wB;
         a0 = fmaf(wA, v.x, a0); a1 = fmaf(wB, v.y, a1);
         a2 = fmaf(wA, v.z, a2); a3 = fmaf(wB, v.w, a3);
     }
 };
 
-template <int W, int S>
+/* MQ = false: one query token per sequence (rows = heads, every row sees [0, L)); the
+ * per-row masks and empty-row guards compile away.  MQ = true: seqlen_q tokens, optional
+ * causal limits per row. */
+template <int W, int S, bool MQ>
 __global__ void __launch_bounds__(W * 32, 1)
 pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
                    const __grid_constant__ CUtensorMap vmap, const DecodeParams p) {
@@ -243,8 +271,8 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
     if (blockIdx.x == 0) {
         for (int b = tid; b < p.B; b += NT) {
             if (pre[b + 1] == pre[b]) {
-                uint4* o4 = reinterpret_cast<uint4*>(p.out + (int64_t)b * p.Hq * kHeadDim);
-                for (int i = 0; i < p.Hq * kHeadDim / 8; ++i) o4[i] = make_uint4(0, 0, 0, 0);
+                uint4* o4 = reinterpret_cast<uint4*>(p.out + (int64_t)b * p.Sq * p.Hq * kHeadDim);
+                for (int i = 0; i < p.Sq * p.Hq * kHeadDim / 8; ++i) o4[i] = make_uint4(0, 0, 0, 0);
             }
         }
     }
@@ -323,13 +351,16 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
 
         uint32_t qf[16];
         int nh_valid = 0;
+        int32_t limA = 0, limB = 0;  // keys visible to this lane's two columns (rows)
         auto load_q = [&](const Cursor& cu) {
             const int32_t kvh = cu.j / p.n_hg;
             const int32_t hg = cu.j - kvh * p.n_hg;
-            nh_valid = min(kHeadsPerGroup, p.g - hg * kHeadsPerGroup);
+            nh_valid = min(kHeadsPerGroup, p.rows - hg * kHeadsPerGroup);
+            limA = row_limit<MQ>(p, hg * kHeadsPerGroup + 2 * tig, cu.L);
+            limB = row_limit<MQ>(p, hg * kHeadsPerGroup + 2 * tig + 1, cu.L);
             if (gid < nh_valid) {
                 const uint32_t* qp = reinterpret_cast<const uint32_t*>(
-                    p.q + ((int64_t)cu.b * p.Hq + kvh * p.g + hg * kHeadsPerGroup + gid) * kHeadDim);
+                    p.q + row_offset<MQ>(p, cu.b, kvh, hg * kHeadsPerGroup + gid));
 #pragma unroll
                 for (int ks = 0; ks < 8; ++ks) {
                     qf[2 * ks] = __ldg(qp + 8 * ks + tig);
@@ -410,7 +441,15 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
             float s[4];
 #pragma unroll
             for (int r = 0; r < 4; ++r) s[r] = (sa[r] + sb[r]) * p.scale_log2;
-            if (nvalid < kChunkTokens) {
+            if (MQ) {
+                // keys past the row's limit (the sequence end, or the causal bound) -> -inf
+                const int32_t t = cc.c * kChunkTokens + gid;
+                s[0] = (t < limA) ? s[0] : -INFINITY;
+                s[1] = (t < limB) ? s[1] : -INFINITY;
+                s[2] = (t + 8 < limA) ? s[2] : -INFINITY;
+                s[3] = (t + 8 < limB) ? s[3] : -INFINITY;
+            } else if (nvalid < kChunkTokens) {
+                // tokens past the sequence end -> -inf (every row sees the same keys)
                 if (gid >= nvalid) { s[0] = -INFINITY; s[1] = -INFINITY; }
                 if (gid + 8 >= nvalid) { s[2] = -INFINITY; s[3] = -INFINITY; }
             }
@@ -425,14 +464,18 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
             }
             const float mnA = fmaxf(m2[0], mxA);
             const float mnB = fmaxf(m2[1], mxB);
-            const float alA = ptx::ex2(m2[0] - mnA);
-            const float alB = ptx::ex2(m2[1] - mnB);
+            // a row with no visible key yet keeps max -inf: exponentiate against 0 instead
+            // (with one query token every chunk holds a visible key for every row)
+            const float bsA = (MQ && mnA == -INFINITY) ? 0.f : mnA;
+            const float bsB = (MQ && mnB == -INFINITY) ? 0.f : mnB;
+            const float alA = ptx::ex2(m2[0] - bsA);
+            const float alB = ptx::ex2(m2[1] - bsB);
             m2[0] = mnA;
             m2[1] = mnB;
-            const float p0 = ptx::ex2(s[0] - mnA);
-            const float p1 = ptx::ex2(s[1] - mnB);
-            const float p2 = ptx::ex2(s[2] - mnA);
-            const float p3 = ptx::ex2(s[3] - mnB);
+            const float p0 = ptx::ex2(s[0] - bsA);
+            const float p1 = ptx::ex2(s[1] - bsB);
+            const float p2 = ptx::ex2(s[2] - bsA);
+            const float p3 = ptx::ex2(s[3] - bsB);
             l2[0] = fmaf(l2[0], alA, p0 + p2);
             l2[1] = fmaf(l2[1], alB, p1 + p3);
 #pragma unroll
@@ -465,13 +508,15 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
                     lA += __shfl_xor_sync(0xffffffffu, lA, off);
                     lB += __shfl_xor_sync(0xffffffffu, lB, off);
                 }
-                const float invA = 1.f / lA, invB = 1.f / lB;
+                // a row with no visible key gives 0 (only with several query tokens)
+                const float invA = (!MQ || lA > 0.f) ? 1.f / lA : 0.f;
+                const float invB = (!MQ || lB > 0.f) ? 1.f / lB : 0.f;
                 const bool full = unit_start_seen && last_of_unit;
                 if (full) {
                     const int32_t kvh = cc.j / p.n_hg;
                     const int32_t hg = cc.j - kvh * p.n_hg;
                     __nv_bfloat16* orow =
-                        p.out + ((int64_t)cc.b * p.Hq + kvh * p.g + hg * kHeadsPerGroup + gid) * kHeadDim;
+                        p.out + row_offset<MQ>(p, cc.b, kvh, hg * kHeadsPerGroup + min(gid, nh_valid - 1));
 #pragma unroll
                     for (int mt = 0; mt < 8; ++mt)
                         store_out_tile(orow, o[mt][0], o[mt][1], o[mt][2], o[mt][3], invA, invB, mt,
@@ -569,10 +614,9 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
         const int64_t ubeg = unit_begin(p, pre, ub, uj);
         const int32_t kvh = uj / p.n_hg;
         const int32_t hg = uj - kvh * p.n_hg;
-        const int nhv = min(kHeadsPerGroup, p.g - hg * kHeadsPerGroup);
+        const int nhv = min(kHeadsPerGroup, p.rows - hg * kHeadsPerGroup);
         const bool inside = (ubeg >= cs && ubeg + n_u <= ce);
-        __nv_bfloat16* orow =
-            p.out + ((int64_t)ub * p.Hq + kvh * p.g + hg * kHeadsPerGroup + gid) * kHeadDim;
+        __nv_bfloat16* orow = p.out + row_offset<MQ>(p, ub, kvh, hg * kHeadsPerGroup + min(gid, nhv - 1));
         for (int mt = warp; mt < 8; mt += W) {
             float2 ls[NF];
             float4 v[NF];
@@ -589,10 +633,12 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
                 bB = in ? fmaxf(bB, ls[f].y) : bB;
             }
             float dA = 0.f, dB = 0.f, a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+            const float zA = (MQ && bA == -INFINITY) ? 0.f : bA;  // rows with no key: weight 0
+            const float zB = (MQ && bB == -INFINITY) ? 0.f : bB;
 #pragma unroll
             for (int f = 0; f < NF; ++f) {
                 const bool in = (run >> f) & 1u;
-                const float wA = ptx::ex2(ls[f].x - bA), wB = ptx::ex2(ls[f].y - bB);
+                const float wA = ptx::ex2(ls[f].x - zA), wB = ptx::ex2(ls[f].y - zB);
                 dA = in ? dA + wA : dA;
                 dB = in ? dB + wB : dB;
                 a0 = in ? fmaf(wA, v[f].x, a0) : a0;
@@ -600,7 +646,8 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
                 a2 = in ? fmaf(wA, v[f].z, a2) : a2;
                 a3 = in ? fmaf(wB, v[f].w, a3) : a3;
             }
-            const float invA = 1.f / dA, invB = 1.f / dB;
+            const float invA = (!MQ || dA > 0.f) ? 1.f / dA : 0.f;
+            const float invB = (!MQ || dB > 0.f) ? 1.f / dB : 0.f;
             if (inside) {
                 store_out_tile(orow, a0, a1, a2, a3, invA, invB, mt, tig, gid < nhv);
                 continue;
@@ -633,7 +680,7 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
             // Record slots: CTA c_first holds the unit's head in slot 2c+1 unless its slice
             // starts exactly at the unit; every later CTA holds it in slot 2c.
             const int64_t slot0 = record_slot(c_first, slice_begin(c_first, nct, T), ubeg);
-            PairMerge g;
+            PairMerge<MQ> g;
             g.init();
             for (int r0 = 0; r0 < nrec; r0 += 16) {
                 float2 lse[16];
@@ -656,7 +703,8 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
                 for (int u = 0; u < 16; ++u)
                     if (r0 + u < nrec) g.add(lse[u].x, lse[u].y, rv[u]);
             }
-            store_out_tile(orow, g.a0, g.a1, g.a2, g.a3, 1.f / g.dA, 1.f / g.dB, mt, tig, gid < nhv);
+            store_out_tile(orow, g.a0, g.a1, g.a2, g.a3, (!MQ || g.dA > 0.f) ? 1.f / g.dA : 0.f,
+                           (!MQ || g.dB > 0.f) ? 1.f / g.dB : 0.f, mt, tig, gid < nhv);
         }
     }
 }
@@ -745,16 +793,18 @@ int64_t workspace_bytes_for(int64_t B, int64_t U, int grid) {
     return (int64_t)s;
 }
 
-int make_plan_impl(int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int64_t P, int sms,
+int make_plan_impl(int64_t B, int64_t Sq, int64_t Hq, int64_t Hkv, int64_t D, int64_t P, int sms,
                    int smem_optin, pgqa_plan* plan) {
     memset(plan, 0, sizeof(*plan));
-    const int st = validate_shape(B, Hq, Hkv, D, P);
+    int st = validate_shape(B, Hq, Hkv, D, P);
+    if (st == PGQA_OK && (Sq <= 0 || Sq > 4096)) st = Sq <= 0 ? PGQA_ERR_BAD_SHAPE : PGQA_ERR_UNSUPPORTED;
     plan->status = st;
     if (st != PGQA_OK) return st;
     if (sms <= 0) sms = kB200Sms;
     if (smem_optin <= 0) smem_optin = kB200SmemOptin;
     const int64_t g = Hq / Hkv;
-    const int64_t n_hg = ceil_div64(g, kHeadsPerGroup);
+    // groups of 8 query rows per KV head; row r = (head r / Sq, token r % Sq)
+    const int64_t n_hg = ceil_div64(g * Sq, kHeadsPerGroup);
     const Knobs& kn = knobs();
     int w = kn.warps > 0 ? kn.warps : kDefaultWarps;
     int s = kn.stages > 0 ? kn.stages : (w == 4 ? 6 : kDefaultStages);
@@ -884,11 +934,11 @@ int lib_workspace(int dev, size_t need, void** out) {
     return PGQA_OK;
 }
 
-template <int W, int S>
+template <int W, int S, bool MQ = false>
 int launch_variant(const CUtensorMap& km, const CUtensorMap& vm, const DecodeParams& p, int grid,
                    int smem, cudaStream_t stream) {
-    auto kern = pgqa_decode_kernel<W, S>;
-    static int configured_smem[kMaxDevices] = {0};
+    auto kern = pgqa_decode_kernel<W, S, MQ>;
+    static int configured_smem[kMaxDevices] = {0};  // one table per instantiation
     int dev = 0;
     cudaGetDevice(&dev);
     if (configured_smem[dev] < smem) {
@@ -917,23 +967,33 @@ int launch_variant(const CUtensorMap& km, const CUtensorMap& vm, const DecodePar
     return PGQA_OK;
 }
 
-int launch(const pgqa_plan& plan, const CUtensorMap& km, const CUtensorMap& vm,
-           const DecodeParams& p, cudaStream_t stream) {
+template <bool MQ>
+int launch_mq(const pgqa_plan& plan, const CUtensorMap& km, const CUtensorMap& vm,
+              const DecodeParams& p, cudaStream_t stream) {
     const int w = plan.warps_per_cta, s = plan.stages;
     const int g = plan.grid_ctas, sm = plan.smem_bytes;
-    if (w == 4 && s == 6) return launch_variant<4, 6>(km, vm, p, g, sm, stream);
-    if (w == 4 && s == 5) return launch_variant<4, 5>(km, vm, p, g, sm, stream);
-    if (w == 4 && s == 4) return launch_variant<4, 4>(km, vm, p, g, sm, stream);
-    if (w == 4 && s == 3) return launch_variant<4, 3>(km, vm, p, g, sm, stream);
-    if (w == 8 && s == 3) return launch_variant<8, 3>(km, vm, p, g, sm, stream);
-    if (w == 8 && s == 2) return launch_variant<8, 2>(km, vm, p, g, sm, stream);
+    if (w == 4 && s == 6) return launch_variant<4, 6, MQ>(km, vm, p, g, sm, stream);
+    if (w == 4 && s == 5) return launch_variant<4, 5, MQ>(km, vm, p, g, sm, stream);
+    if (w == 4 && s == 4) return launch_variant<4, 4, MQ>(km, vm, p, g, sm, stream);
+    if (w == 4 && s == 3) return launch_variant<4, 3, MQ>(km, vm, p, g, sm, stream);
+    if (w == 8 && s == 3) return launch_variant<8, 3, MQ>(km, vm, p, g, sm, stream);
+    if (w == 8 && s == 2) return launch_variant<8, 2, MQ>(km, vm, p, g, sm, stream);
     return PGQA_ERR_UNSUPPORTED;
 }
 
+/* One query token (causal or not: an end-aligned mask hides nothing) takes the
+ * single-token instantiation. */
+int launch(const pgqa_plan& plan, const CUtensorMap& km, const CUtensorMap& vm,
+           const DecodeParams& p, cudaStream_t stream) {
+    return p.Sq > 1 ? launch_mq<true>(plan, km, vm, p, stream)
+                    : launch_mq<false>(plan, km, vm, p, stream);
+}
+
 int decode_impl(const void* q, const void* k, const void* v, void* out, const int32_t* seq_lens,
-                const int32_t* bt, int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int64_t P,
-                int64_t num_pages, int64_t bt_stride, int64_t max_seqlen, float scale,
-                void* workspace, size_t ws_bytes, cudaStream_t stream) {
+                const int32_t* bt, int64_t B, int64_t Sq, int64_t Hq, int64_t Hkv, int64_t D,
+                int64_t P, int64_t num_pages, int64_t bt_stride, int64_t max_seqlen,
+                int64_t causal, float scale, void* workspace, size_t ws_bytes,
+                cudaStream_t stream) {
     if (!q || !k || !v || !out || !seq_lens || !bt) return PGQA_ERR_NULL_POINTER;
     int st = validate_shape(B, Hq, Hkv, D, P);
     if (st != PGQA_OK) return st;
@@ -942,6 +1002,7 @@ int decode_impl(const void* q, const void* k, const void* v, void* out, const in
     const int64_t cap = bt_stride * P;
     if (max_seqlen < 0 || max_seqlen > cap) return PGQA_ERR_BAD_SHAPE;
     if (!(scale > 0.f) || !isfinite(scale)) return PGQA_ERR_BAD_SHAPE;
+    if (causal != 0 && causal != 1) return PGQA_ERR_BAD_SHAPE;
     if ((reinterpret_cast<uintptr_t>(k) & 15) || (reinterpret_cast<uintptr_t>(v) & 15) ||
         (reinterpret_cast<uintptr_t>(q) & 15) || (reinterpret_cast<uintptr_t>(out) & 15) ||
         (reinterpret_cast<uintptr_t>(seq_lens) & 3) || (reinterpret_cast<uintptr_t>(bt) & 3))
@@ -956,7 +1017,7 @@ int decode_impl(const void* q, const void* k, const void* v, void* out, const in
     st = device_info(dev, &di);
     if (st != PGQA_OK) return st;
     pgqa_plan plan;
-    st = make_plan_impl(B, Hq, Hkv, D, P, di.sms, di.smem_optin, &plan);
+    st = make_plan_impl(B, Sq, Hq, Hkv, D, P, di.sms, di.smem_optin, &plan);
     if (st != PGQA_OK) return st;
 
     if (workspace == nullptr) {
@@ -993,6 +1054,9 @@ int decode_impl(const void* q, const void* k, const void* v, void* out, const in
     p.g = (int32_t)g;
     p.n_hg = plan.head_groups;
     p.U = plan.units_per_seq;
+    p.Sq = (int32_t)Sq;
+    p.rows = (int32_t)(g * Sq);
+    p.causal = (int32_t)causal;
     p.page_size = (int32_t)P;
     p.bt_stride = (int32_t)bt_stride;
     p.num_pages = (int32_t)num_pages;
@@ -1031,10 +1095,10 @@ extern "C" void run_kernel(const void* q, const void* k_cache_paged, const void*
         set_status(PGQA_ERR_BAD_SHAPE);
         return;
     }
-    // One query token: a causal mask aligned to the sequence end hides nothing, so
-    // causal = 0 and causal = 1 give the same result.
-    if (seqlen_q != 1 || (causal != 0 && causal != 1)) {
-        set_status(PGQA_ERR_UNSUPPORTED);
+    // seqlen_q query tokens per sequence; causal aligns the mask to the end of the
+    // cache (token i sees keys [0, L - seqlen_q + i]).  With one token it hides nothing.
+    if (seqlen_q <= 0 || (causal != 0 && causal != 1)) {
+        set_status(seqlen_q <= 0 ? PGQA_ERR_BAD_SHAPE : PGQA_ERR_UNSUPPORTED);
         return;
     }
     const int64_t stride = num_blocks / batch_size;
@@ -1044,8 +1108,9 @@ extern "C" void run_kernel(const void* q, const void* k_cache_paged, const void*
     }
     const float scale = 1.0f / sqrtf((float)headdim);
     set_status(decode_impl(q, k_cache_paged, v_cache_paged, output, cache_seqlens, block_table,
-                           batch_size, num_heads, num_heads_k, headdim, page_block_size,
-                           num_blocks, stride, seqlen_k, scale, nullptr, 0, (cudaStream_t)0));
+                           batch_size, seqlen_q, num_heads, num_heads_k, headdim, page_block_size,
+                           num_blocks, stride, seqlen_k, causal, scale, nullptr, 0,
+                           (cudaStream_t)0));
 }
 
 extern "C" int pgqa_decode_v1(const void* q, const void* k_cache, const void* v_cache, void* out,
@@ -1054,14 +1119,27 @@ extern "C" int pgqa_decode_v1(const void* q, const void* k_cache, const void* v_
                               int64_t headdim, int64_t page_size, int64_t num_pages,
                               int64_t bt_stride, int64_t max_seqlen, float scale,
                               void* workspace, size_t workspace_bytes, void* stream) {
-    return set_status(decode_impl(q, k_cache, v_cache, out, seq_lens, block_table, batch_size,
+    return set_status(decode_impl(q, k_cache, v_cache, out, seq_lens, block_table, batch_size, 1,
                                   num_heads, num_heads_k, headdim, page_size, num_pages, bt_stride,
-                                  max_seqlen, scale, workspace, workspace_bytes,
+                                  max_seqlen, 0, scale, workspace, workspace_bytes,
                                   static_cast<cudaStream_t>(stream)));
 }
 
-extern "C" size_t pgqa_workspace_size(int64_t batch_size, int64_t num_heads, int64_t num_heads_k,
-                                      int64_t headdim, int64_t page_size) {
+extern "C" int pgqa_decode_v2(const void* q, const void* k_cache, const void* v_cache, void* out,
+                              const int32_t* seq_lens, const int32_t* block_table,
+                              int64_t batch_size, int64_t seqlen_q, int64_t num_heads,
+                              int64_t num_heads_k, int64_t headdim, int64_t page_size,
+                              int64_t num_pages, int64_t bt_stride, int64_t max_seqlen,
+                              int64_t causal, float scale, void* workspace,
+                              size_t workspace_bytes, void* stream) {
+    return set_status(decode_impl(q, k_cache, v_cache, out, seq_lens, block_table, batch_size,
+                                  seqlen_q, num_heads, num_heads_k, headdim, page_size, num_pages,
+                                  bt_stride, max_seqlen, causal, scale, workspace,
+                                  workspace_bytes, static_cast<cudaStream_t>(stream)));
+}
+
+static size_t workspace_size_impl(int64_t batch_size, int64_t seqlen_q, int64_t num_heads,
+                                  int64_t num_heads_k, int64_t headdim, int64_t page_size) {
     int sms = 0, optin = 0;
     int dev = 0;
     DevInfo di;
@@ -1072,10 +1150,20 @@ extern "C" size_t pgqa_workspace_size(int64_t batch_size, int64_t num_heads, int
         cudaGetLastError();
     }
     pgqa_plan plan;
-    if (make_plan_impl(batch_size, num_heads, num_heads_k, headdim, page_size, sms, optin, &plan) !=
-        PGQA_OK)
+    if (make_plan_impl(batch_size, seqlen_q, num_heads, num_heads_k, headdim, page_size, sms, optin,
+                       &plan) != PGQA_OK)
         return 0;
     return (size_t)plan.workspace_bytes;
+}
+
+extern "C" size_t pgqa_workspace_size(int64_t batch_size, int64_t num_heads, int64_t num_heads_k,
+                                      int64_t headdim, int64_t page_size) {
+    return workspace_size_impl(batch_size, 1, num_heads, num_heads_k, headdim, page_size);
+}
+
+extern "C" size_t pgqa_workspace_size_v2(int64_t batch_size, int64_t seqlen_q, int64_t num_heads,
+                                         int64_t num_heads_k, int64_t headdim, int64_t page_size) {
+    return workspace_size_impl(batch_size, seqlen_q, num_heads, num_heads_k, headdim, page_size);
 }
 
 extern "C" int pgqa_workspace_init(void* workspace, size_t workspace_bytes, void* stream) {
@@ -1141,7 +1229,7 @@ extern "C" int pgqa_make_plan(int64_t batch_size, int64_t num_heads, int64_t num
                               int64_t headdim, int64_t page_size, int32_t num_sms,
                               int32_t smem_per_block_optin, pgqa_plan* plan) {
     if (plan == nullptr) return PGQA_ERR_NULL_POINTER;
-    return make_plan_impl(batch_size, num_heads, num_heads_k, headdim, page_size, num_sms,
+    return make_plan_impl(batch_size, 1, num_heads, num_heads_k, headdim, page_size, num_sms,
                           smem_per_block_optin, plan);
 }
 
@@ -1247,7 +1335,7 @@ extern "C" int pgqa_decode_noalloc(const void* q, const void* k_cache, const voi
     int st = device_info(dev, &di);
     if (st != PGQA_OK) return set_status(st);
     pgqa_plan plan;
-    st = make_plan_impl(batch_size, num_heads, num_heads_k, headdim, page_size, di.sms,
+    st = make_plan_impl(batch_size, 1, num_heads, num_heads_k, headdim, page_size, di.sms,
                         di.smem_optin, &plan);
     if (st != PGQA_OK) return set_status(st);
     if ((size_t)plan.workspace_bytes > kNoAllocScratchBytes)
@@ -1266,9 +1354,9 @@ extern "C" int pgqa_decode_noalloc(const void* q, const void* k_cache, const voi
         cudaGetLastError();
         return set_status(PGQA_ERR_CUDA);
     }
-    return set_status(decode_impl(q, k_cache, v_cache, out, seq_lens, block_table, batch_size,
+    return set_status(decode_impl(q, k_cache, v_cache, out, seq_lens, block_table, batch_size, 1,
                                   num_heads, num_heads_k, headdim, page_size, num_pages,
-                                  bt_stride, max_seqlen, scale, scratch, kNoAllocScratchBytes,
+                                  bt_stride, max_seqlen, 0, scale, scratch, kNoAllocScratchBytes,
                                   s));
 }
 

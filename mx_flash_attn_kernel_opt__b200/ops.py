@@ -29,15 +29,16 @@ def _stream_handle(device):
     return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
 
 
-def workspace_for(batch_size, num_heads, num_heads_k, headdim, page_size, device):
-    """A zero-initialised workspace tensor for pgqa_decode_v1, cached per device/shape."""
+def workspace_for(batch_size, num_heads, num_heads_k, headdim, page_size, device, seqlen_q=1):
+    """A zero-initialised workspace tensor for the decode entry points, cached per device
+    (grown when a larger shape needs more)."""
     L = lib()
     dev = torch.device(device)
     with torch.cuda.device(dev):
-        need = L.pgqa_workspace_size(batch_size, num_heads, num_heads_k, headdim, page_size)
+        need = L.pgqa_workspace_size_v2(batch_size, seqlen_q, num_heads, num_heads_k, headdim,
+                                        page_size)
     if need == 0:
-        raise PgqaError(2, "pgqa_workspace_size")
-    key = (dev.index, need)
+        raise PgqaError(2, "pgqa_workspace_size_v2")
     ws = _workspaces.get(dev.index)
     if ws is None or ws.numel() < need:
         ws = torch.zeros(max(need, 1 << 20), dtype=torch.uint8, device=dev)
@@ -59,19 +60,20 @@ def _check_tensors(q, k, v, out, seq_lens, block_table):
 
 
 def decode(q, k_cache, v_cache, block_table, seq_lens, scale=None, out=None,
-           max_seqlen=0, workspace=None):
+           max_seqlen=0, workspace=None, causal=False):
     """Paged GQA decode.
 
-    q [B, Hq, D] or [B, 1, Hq, D]; k_cache/v_cache [num_pages, P, Hkv, D] (bf16);
-    block_table [B, stride] int32; seq_lens [B] int32.  Returns out (same shape as q).
+    q [B, Hq, D] (one query token) or [B, Sq, Hq, D]; k_cache/v_cache
+    [num_pages, P, Hkv, D] (bf16); block_table [B, stride] int32; seq_lens [B] int32.
+    With Sq > 1 and `causal`, query token i sees keys [0, L - Sq + i].  Returns out (same
+    shape as q).
     """
     if out is None:
         out = torch.empty_like(q)
     _check_tensors(q, k_cache, v_cache, out, seq_lens, block_table)
     B = q.shape[0]
     Hq, D = q.shape[-2], q.shape[-1]
-    if q.dim() == 4 and q.shape[1] != 1:
-        raise PgqaError(3, "decode: seqlen_q must be 1")
+    Sq = q.shape[1] if q.dim() == 4 else 1
     num_pages, P, Hkv, Dk = k_cache.shape
     if tuple(v_cache.shape) != tuple(k_cache.shape) or Dk != D:
         raise PgqaError(2, "decode: K/V pool shapes")
@@ -80,14 +82,14 @@ def decode(q, k_cache, v_cache, block_table, seq_lens, scale=None, out=None,
     if scale is None:
         scale = 1.0 / math.sqrt(D)
     if workspace is None:
-        workspace = workspace_for(B, Hq, Hkv, D, P, q.device)
+        workspace = workspace_for(B, Hq, Hkv, D, P, q.device, seqlen_q=Sq)
     L = lib()
     with torch.cuda.device(q.device):
-        st = L.pgqa_decode_v1(_ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(out), _ptr(seq_lens),
-                              _ptr(block_table), B, Hq, Hkv, D, P, num_pages,
-                              block_table.stride(0), max_seqlen, float(scale),
+        st = L.pgqa_decode_v2(_ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(out), _ptr(seq_lens),
+                              _ptr(block_table), B, Sq, Hq, Hkv, D, P, num_pages,
+                              block_table.stride(0), max_seqlen, int(bool(causal)), float(scale),
                               _ptr(workspace), workspace.numel(), _stream_handle(q.device))
-    check(st, "pgqa_decode_v1")
+    check(st, "pgqa_decode_v2")
     return out
 
 
@@ -98,18 +100,19 @@ def run_kernel(q, k_cache_paged, v_cache_paged, output, cache_seqlens, block_tab
     batch_size, num_blocks = int(batch_size), int(num_blocks)
     if batch_size <= 0 or num_blocks % batch_size != 0:
         raise PgqaError(2, "run_kernel: num_blocks must be a multiple of batch_size")
-    if int(seqlen_q) != 1 or int(causal) not in (0, 1):
-        raise PgqaError(3, "run_kernel: only seqlen_q == 1 decode is supported")
+    if int(seqlen_q) < 1 or int(causal) not in (0, 1):
+        raise PgqaError(2, "run_kernel: seqlen_q must be >= 1 and causal 0 or 1")
     stride = num_blocks // batch_size
     if int(seqlen_k) > stride * int(page_block_size):
         raise PgqaError(2, "run_kernel: seqlen_k exceeds the block-table capacity")
-    q3 = q.view(batch_size, int(num_heads), int(headdim))
-    o3 = output.view(batch_size, int(num_heads), int(headdim))
+    shape = (batch_size, int(seqlen_q), int(num_heads), int(headdim))
+    q4 = q.view(shape)
+    o4 = output.view(shape)
     k = k_cache_paged.view(num_blocks, int(page_block_size), int(num_heads_k), int(headdim))
     v = v_cache_paged.view(num_blocks, int(page_block_size), int(num_heads_k), int(headdim))
     bt = block_table.view(batch_size, stride)
-    decode(q3, k, v, bt, cache_seqlens, scale=1.0 / math.sqrt(int(headdim)), out=o3,
-           max_seqlen=int(seqlen_k))
+    decode(q4, k, v, bt, cache_seqlens, scale=1.0 / math.sqrt(int(headdim)), out=o4,
+           max_seqlen=int(seqlen_k), causal=bool(int(causal)))
     return output
 
 

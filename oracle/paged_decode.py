@@ -3,7 +3,10 @@
 paged_decode_ref restates the operator's mathematical definition (task.md:138-147) and
 its token -> page mapping (task.md:94,146): for sequence b only the first
 ceil(L_b / P) block-table entries are read, token t is slot t % P of page
-block_table[b, t // P], and query head h reads KV head h // (Hq / Hkv).
+block_table[b, t // P], and query head h reads KV head h // (Hq / Hkv).  Beyond the
+reference's seqlen_q = 1 it also restates several query tokens per sequence with the
+end-aligned causal mask of flash_attn_with_kvcache (the reference's comparison target,
+task.md:16-26), which the run_kernel ABI can express through seqlen_q and causal.
 
 split_partials_ref / lse_combine_ref restate the split-KV online softmax with a
 running max (optimized_c500_flash_attn.cu:370-423: page max, alpha = exp(m_old - m_new),
@@ -30,19 +33,26 @@ def _gather_seq(k_cache, v_cache, block_table, b, L):
     return K, V
 
 
-def paged_decode_ref(q, k_cache, v_cache, block_table, seq_lens, scale=None, rows=None):
-    """fp32 reference.  q [B, Hq, D] (or [B,1,Hq,D]); pools [num_pages, P, Hkv, D].
-    Returns fp32 [B, Hq, D] (zeros for L_b == 0).  `rows` limits the work to the given
+def paged_decode_ref(q, k_cache, v_cache, block_table, seq_lens, scale=None, rows=None,
+                     causal=False):
+    """fp32 reference.  q [B, Hq, D] (one query token) or [B, Sq, Hq, D]; pools
+    [num_pages, P, Hkv, D].  Returns fp32 of q's shape.
+
+    With Sq query tokens, token i of sequence b sees keys [0, L_b) -- or, when `causal`,
+    keys [0, L_b - Sq + i] (the mask aligned to the end of the cache, as
+    flash_attn_with_kvcache defines it).  A query with no visible key (L_b == 0, or
+    causal with L_b - Sq + i < 0) gives zeros.  `rows` limits the work to the given
     sequence indices (the other rows stay zero)."""
-    q = q.reshape(q.shape[0], q.shape[-2], q.shape[-1]).cpu()
+    squeeze = q.dim() == 3
+    q4 = (q.unsqueeze(1) if squeeze else q).cpu()
     k_cache, v_cache = k_cache.cpu(), v_cache.cpu()
     block_table, seq_lens = block_table.cpu(), seq_lens.cpu()
-    B, Hq, D = q.shape
+    B, Sq, Hq, D = q4.shape
     Hkv = k_cache.shape[2]
     g = Hq // Hkv
     if scale is None:
         scale = 1.0 / math.sqrt(D)
-    out = torch.zeros(B, Hq, D, dtype=torch.float32)
+    out = torch.zeros(B, Sq, Hq, D, dtype=torch.float32)
     for b in (range(B) if rows is None else rows):
         L = int(seq_lens[b])
         if L <= 0:
@@ -50,11 +60,15 @@ def paged_decode_ref(q, k_cache, v_cache, block_table, seq_lens, scale=None, row
         K, V = _gather_seq(k_cache, v_cache, block_table, b, L)
         Kt = K.float().permute(1, 2, 0)            # [Hkv, D, L]
         Vt = V.float().permute(1, 0, 2)            # [Hkv, L, D]
-        qb = q[b].float().reshape(Hkv, g, D)       # head h -> kv h // g
-        s = torch.bmm(qb, Kt) * scale              # [Hkv, g, L]
-        p = torch.softmax(s, dim=-1)
-        out[b] = torch.bmm(p, Vt).reshape(Hq, D)
-    return out
+        for i in range(Sq):
+            n = L if not causal else min(L, L - Sq + i + 1)
+            if n <= 0:
+                continue
+            qb = q4[b, i].float().reshape(Hkv, g, D)   # head h -> kv h // g
+            s = torch.bmm(qb, Kt[:, :, :n]) * scale    # [Hkv, g, n]
+            p = torch.softmax(s, dim=-1)
+            out[b, i] = torch.bmm(p, Vt[:, :n]).reshape(Hq, D)
+    return out[:, 0] if squeeze else out
 
 
 LOG2E = 1.4426950408889634

@@ -24,7 +24,7 @@ def declared_functions():
 def test_header_declares_the_reference_symbol():
     names = declared_functions()
     assert "run_kernel" in names
-    assert {"pgqa_decode_v1", "pgqa_workspace_size", "pgqa_make_plan"} <= set(names)
+    assert {"pgqa_decode_v1", "pgqa_decode_v2", "pgqa_workspace_size", "pgqa_make_plan"} <= set(names)
 
 
 def test_library_loads_and_exports_every_declared_symbol():
@@ -116,8 +116,10 @@ def test_reference_entry_validates_arguments():
     assert L.pgqa_last_status() == 2              # batch_size 0
     L.run_kernel(*args, 4, 16, 1, 32, 8, 128, 16, 63, 0)
     assert L.pgqa_last_status() == 2              # num_blocks % batch_size
-    L.run_kernel(*args, 4, 16, 2, 32, 8, 128, 16, 64, 0)
-    assert L.pgqa_last_status() == 3              # seqlen_q != 1
+    L.run_kernel(*args, 4, 16, 0, 32, 8, 128, 16, 64, 0)
+    assert L.pgqa_last_status() == 2              # seqlen_q < 1
+    L.run_kernel(*args, 4, 16, 1, 32, 8, 128, 16, 64, 2)
+    assert L.pgqa_last_status() == 3              # causal not 0 / 1
     L.run_kernel(*args, 4, 1000, 1, 32, 8, 128, 16, 64, 0)
     assert L.pgqa_last_status() == 2              # seqlen_k above table capacity
     L.run_kernel(*args, 4, 16, 1, 32, 8, 96, 16, 64, 0)
@@ -128,3 +130,6 @@ def test_workspace_size_is_zero_for_invalid_shapes():
     L = _lib.lib()
     assert L.pgqa_workspace_size(0, 32, 8, 128, 16) == 0
     assert L.pgqa_workspace_size(4, 32, 8, 128, 16) > 0
+    assert L.pgqa_workspace_size_v2(4, 0, 32, 8, 128, 16) == 0
+    # more query tokens -> more row groups per KV head -> more arrival counters
+    assert L.pgqa_workspace_size_v2(4, 4, 32, 8, 128, 16) > L.pgqa_workspace_size(4, 32, 8, 128, 16)

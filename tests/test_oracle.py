@@ -79,3 +79,22 @@ def test_match_stats_rule():
     assert math.isclose(frac, 0.99, abs_tol=1e-6) and not outlier
     out[1] += 1.0
     assert match_stats(out, ref)[1]
+
+
+def test_oracle_multi_query_restates_single_token():
+    """Sq query tokens: non-causal = Sq independent single-token decodes over L keys;
+    causal token i = single-token decode over the first L - Sq + i + 1 keys."""
+    from mx_flash_attn_kernel_opt__b200 import inputs
+    Sq = 3
+    inp = inputs.custom_case(4, 8, 2, 16, [1, 2, 40, 7], seed=6, width=4)
+    q = torch.randn(4, Sq, 8, 128, generator=torch.Generator().manual_seed(2)).to(torch.bfloat16)
+    full = paged_decode_ref(q, inp.k, inp.v, inp.block_table, inp.seq_lens)
+    causal = paged_decode_ref(q, inp.k, inp.v, inp.block_table, inp.seq_lens, causal=True)
+    for i in range(Sq):
+        one = paged_decode_ref(q[:, i], inp.k, inp.v, inp.block_table, inp.seq_lens)
+        assert torch.allclose(full[:, i], one, atol=1e-6)
+        trunc = (inp.seq_lens - Sq + i + 1).clamp(min=0).to(torch.int32)
+        one = paged_decode_ref(q[:, i], inp.k, inp.v, inp.block_table, trunc)
+        assert torch.allclose(causal[:, i], one, atol=1e-6)
+    # L = 1 with 3 causal tokens: tokens 0 and 1 see nothing
+    assert torch.count_nonzero(causal[0, :2]) == 0 and torch.count_nonzero(causal[0, 2]) > 0
