@@ -103,6 +103,36 @@ int pgqa_decode_v2(const void* q, const void* k_cache, const void* v_cache, void
                    void* stream);
 
 /*
+ * Append-KV step (no counterpart symbol in the reference; it is the k / v argument pair
+ * of flash_attn_with_kvcache, which the reference's task passes as None, task.md:16-26).
+ * Writes k_new / v_new [B, seqlen_new, Hkv, D] bf16 into the pools at token positions
+ * [L_b, L_b + seqlen_new) of each sequence, L_b = seq_lens[b] being the length BEFORE
+ * the append; token t goes to slot t % P of page block_table[b, t / P].  seq_lens is
+ * not modified (the caller advances it).  Positions past the table capacity or page ids
+ * outside [0, num_pages) are skipped and flagged in the device error word of
+ * `workspace` (the library's own when NULL; read with pgqa_check_device_error).
+ * Asynchronous on `stream`.
+ */
+int pgqa_append_kv(const void* k_new, const void* v_new, void* k_cache, void* v_cache,
+                   const int32_t* seq_lens, const int32_t* block_table, int64_t batch_size,
+                   int64_t seqlen_new, int64_t num_heads_k, int64_t headdim, int64_t page_size,
+                   int64_t num_pages, int64_t bt_stride, void* workspace, void* stream);
+
+/*
+ * pgqa_append_kv followed by pgqa_decode_v2 over the extended sequences, in one call
+ * (flash_attn_with_kvcache with k / v given; no counterpart symbol in the reference).
+ * Sequence b is attended over L_b + seqlen_new keys; with causal = 1 query token i sees
+ * keys [0, L_b + seqlen_new - seqlen_q + i].  seqlen_new = 0 is plain pgqa_decode_v2.
+ */
+int pgqa_decode_kvcache(const void* q, void* k_cache, void* v_cache, const void* k_new,
+                        const void* v_new, void* out, const int32_t* seq_lens,
+                        const int32_t* block_table, int64_t batch_size, int64_t seqlen_q,
+                        int64_t seqlen_new, int64_t num_heads, int64_t num_heads_k,
+                        int64_t headdim, int64_t page_size, int64_t num_pages, int64_t bt_stride,
+                        int64_t max_seqlen, int64_t causal, float scale, void* workspace,
+                        size_t workspace_bytes, void* stream);
+
+/*
  * Allocation-free variant of pgqa_decode_v1 (no counterpart in the reference).
  *
  * Some callers cannot allocate device memory when they call the decode: code running

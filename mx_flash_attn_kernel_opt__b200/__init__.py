@@ -5,10 +5,13 @@ libpgqa.so in this directory).  Python entry points:
 
   run_kernel(...)       the reference's operator surface (tensors + 9 integers)
   run_kernel_cabi(...)  the raw C symbol through ctypes, as the reference harness calls it
-  decode(...)           general form: explicit scale, pool size and table stride
+  decode(...)           general form: explicit scale, pool size and table stride,
+                        several query tokens, optional append of new K/V tokens
+  append_kv(...)        the append-KV step alone
 """
 from ._lib import LIB_PATH, PgqaError, lib  # noqa: F401
 from .ops import (  # noqa: F401
+    append_kv,
     check_device_error,
     decode,
     make_plan,
@@ -17,5 +20,5 @@ from .ops import (  # noqa: F401
     workspace_for,
 )
 
-__all__ = ["run_kernel", "run_kernel_cabi", "decode", "make_plan", "check_device_error",
+__all__ = ["run_kernel", "run_kernel_cabi", "decode", "append_kv", "make_plan", "check_device_error",
            "workspace_for", "PgqaError", "lib", "LIB_PATH"]

@@ -8,8 +8,9 @@ import sys
 PKG_DIR = os.path.dirname(os.path.abspath(__file__))
 REPO_DIR = os.path.dirname(PKG_DIR)
 CSRC = os.path.join(PKG_DIR, "csrc")
-SOURCES = [os.path.join(CSRC, "pgqa_decode.cu")]
+SOURCES = [os.path.join(CSRC, "pgqa_decode.cu"), os.path.join(CSRC, "pgqa_append.cu")]
 DEPS = SOURCES + [
+    os.path.join(CSRC, "pgqa_append.h"),
     os.path.join(CSRC, "pgqa_partition.h"),
     os.path.join(CSRC, "pgqa_ptx.cuh"),
     os.path.join(REPO_DIR, "include", "pgqa.h"),

@@ -43,6 +43,7 @@
 #include <mutex>
 
 #include "../../include/pgqa.h"
+#include "pgqa_append.h"
 #include "pgqa_partition.h"
 #include "pgqa_ptx.cuh"
 
@@ -57,6 +58,8 @@ constexpr int kHalfBytes = 2048;           // 16 tokens x 64 dims x bf16
 constexpr uint64_t kWaitLimitNs = 1000000000ull;  // 1 s bound on any single wait
 
 enum DeviceErr : int32_t { kErrTimeout = 1, kErrBadPage = 2, kErrBadSeqlen = 4 };
+static_assert(kErrBadPage == kAppendBadPage && kErrBadSeqlen == kAppendBadSeqlen,
+              "the append step shares the decode's error word");
 
 struct DecodeParams {
     const __nv_bfloat16* q;
@@ -71,6 +74,7 @@ struct DecodeParams {
     int32_t Sq;      // query tokens per sequence
     int32_t rows;    // query rows per KV head = g * Sq (row r: head r / Sq, token r % Sq)
     int32_t causal;  // query token i sees keys [0, L - Sq + i] instead of [0, L)
+    int32_t len_add; // tokens appended by this call: sequence b has seq_lens[b] + len_add keys
     int32_t page_size, bt_stride, num_pages;
     int64_t cap_tokens;  // bt_stride * page_size (clamp for seq_lens)
     float scale_log2;    // scale * log2(e)
@@ -92,10 +96,15 @@ struct Cursor {
     int32_t b, j, c, n, L;  // sequence, unit-in-sequence, chunk-in-unit, chunks, length
 };
 
-__device__ __forceinline__ int32_t clamp_len(int32_t L, int64_t cap) {
+__device__ __forceinline__ int32_t clamp_len(int64_t L, int64_t cap) {
     if (L < 0) return 0;
-    if ((int64_t)L > cap) return (int32_t)cap;
-    return L;
+    if (L > cap) return (int32_t)cap;
+    return (int32_t)L;
+}
+
+/* Keys of sequence b: its entry in seq_lens plus the tokens appended by this call. */
+__device__ __forceinline__ int64_t keys_of(const DecodeParams& p, int32_t b) {
+    return (int64_t)__ldg(p.seq_lens + b) + p.len_add;
 }
 
 /* Largest b with pre[b]*U <= x  (x < pre[B]*U). */
@@ -115,7 +124,7 @@ __device__ __forceinline__ Cursor locate(const DecodeParams& p, const uint32_t* 
     const int64_t r = x - (int64_t)pre[cu.b] * p.U;
     cu.j = (int32_t)(r / cu.n);
     cu.c = (int32_t)(r - (int64_t)cu.j * cu.n);
-    cu.L = clamp_len(__ldg(p.seq_lens + cu.b), p.cap_tokens);
+    cu.L = clamp_len(keys_of(p, cu.b), p.cap_tokens);
     return cu;
 }
 
@@ -127,7 +136,7 @@ __device__ __forceinline__ void advance(const DecodeParams& p, const uint32_t* p
     cu.j = 0;
     do { ++cu.b; } while (pre[cu.b + 1] == pre[cu.b]);
     cu.n = (int32_t)(pre[cu.b + 1] - pre[cu.b]);
-    cu.L = clamp_len(__ldg(p.seq_lens + cu.b), p.cap_tokens);
+    cu.L = clamp_len(keys_of(p, cu.b), p.cap_tokens);
 }
 
 __device__ __forceinline__ int64_t unit_begin(const DecodeParams& p, const uint32_t* pre, int32_t b,
@@ -243,8 +252,9 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
         uint32_t local = 0;
         int32_t bad = 0;
         for (int b = b0; b < b1; ++b) {
-            const int32_t L = __ldg(p.seq_lens + b);
-            if (L < 0 || (int64_t)L > p.cap_tokens) bad = 1;
+            const int32_t L0 = __ldg(p.seq_lens + b);
+            const int64_t L = (int64_t)L0 + p.len_add;
+            if (L0 < 0 || L > p.cap_tokens) bad = 1;
             local += (uint32_t)seq_chunks(L, p.cap_tokens);
         }
         if (bad && blockIdx.x == 0) atomicOr(p.err, kErrBadSeqlen);
@@ -261,7 +271,7 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
         uint32_t run = base + incl - local;
         for (int b = b0; b < b1; ++b) {
             pre[b] = run;
-            run += (uint32_t)seq_chunks(__ldg(p.seq_lens + b), p.cap_tokens);
+            run += (uint32_t)seq_chunks(keys_of(p, b), p.cap_tokens);
         }
         if (tid == NT - 1) pre[p.B] = base + incl;
         __syncthreads();
@@ -993,8 +1003,13 @@ int decode_impl(const void* q, const void* k, const void* v, void* out, const in
                 const int32_t* bt, int64_t B, int64_t Sq, int64_t Hq, int64_t Hkv, int64_t D,
                 int64_t P, int64_t num_pages, int64_t bt_stride, int64_t max_seqlen,
                 int64_t causal, float scale, void* workspace, size_t ws_bytes,
-                cudaStream_t stream) {
+                cudaStream_t stream, const void* k_new = nullptr, const void* v_new = nullptr,
+                int64_t len_add = 0) {
     if (!q || !k || !v || !out || !seq_lens || !bt) return PGQA_ERR_NULL_POINTER;
+    if (len_add < 0 || len_add > 4096) return len_add < 0 ? PGQA_ERR_BAD_SHAPE : PGQA_ERR_UNSUPPORTED;
+    if (len_add > 0 && (!k_new || !v_new)) return PGQA_ERR_NULL_POINTER;
+    if ((reinterpret_cast<uintptr_t>(k_new) & 15) || (reinterpret_cast<uintptr_t>(v_new) & 15))
+        return PGQA_ERR_MISALIGNED;
     int st = validate_shape(B, Hq, Hkv, D, P);
     if (st != PGQA_OK) return st;
     if (num_pages <= 0 || bt_stride <= 0) return PGQA_ERR_BAD_SHAPE;
@@ -1057,6 +1072,7 @@ int decode_impl(const void* q, const void* k, const void* v, void* out, const in
     p.Sq = (int32_t)Sq;
     p.rows = (int32_t)(g * Sq);
     p.causal = (int32_t)causal;
+    p.len_add = (int32_t)len_add;
     p.page_size = (int32_t)P;
     p.bt_stride = (int32_t)bt_stride;
     p.num_pages = (int32_t)num_pages;
@@ -1071,6 +1087,26 @@ int decode_impl(const void* q, const void* k, const void* v, void* out, const in
         const char* lim = getenv("PGQA_WAIT_LIMIT_NS");
         p.wait_limit_ns = (lim && *lim) ? strtoull(lim, nullptr, 10) : kWaitLimitNs;
         if (p.wait_limit_ns == 0 || p.wait_limit_ns > 10 * kWaitLimitNs) p.wait_limit_ns = kWaitLimitNs;
+    }
+    if (len_add > 0) {
+        // Append first; the decode launches as its programmatic dependent and its
+        // griddepcontrol.wait orders every read of the pool after the append's writes.
+        AppendArgs a;
+        a.k_new = static_cast<const uint4*>(k_new);
+        a.v_new = static_cast<const uint4*>(v_new);
+        a.k_cache = static_cast<uint4*>(const_cast<void*>(k));
+        a.v_cache = static_cast<uint4*>(const_cast<void*>(v));
+        a.seq_lens = seq_lens;
+        a.block_table = bt;
+        a.err = p.err;
+        a.B = (int32_t)B;
+        a.S_new = (int32_t)len_add;
+        a.Hkv = (int32_t)Hkv;
+        a.P = (int32_t)P;
+        a.bt_stride = (int32_t)bt_stride;
+        a.num_pages = (int32_t)num_pages;
+        a.cap_tokens = cap;
+        if (launch_append(a, di.sms, stream) != 0) return PGQA_ERR_CUDA;
     }
     return launch(plan, km, vm, p, stream);
 }
@@ -1136,6 +1172,71 @@ extern "C" int pgqa_decode_v2(const void* q, const void* k_cache, const void* v_
                                   seqlen_q, num_heads, num_heads_k, headdim, page_size, num_pages,
                                   bt_stride, max_seqlen, causal, scale, workspace,
                                   workspace_bytes, static_cast<cudaStream_t>(stream)));
+}
+
+extern "C" int pgqa_decode_kvcache(const void* q, void* k_cache, void* v_cache,
+                                   const void* k_new, const void* v_new, void* out,
+                                   const int32_t* seq_lens, const int32_t* block_table,
+                                   int64_t batch_size, int64_t seqlen_q, int64_t seqlen_new,
+                                   int64_t num_heads, int64_t num_heads_k, int64_t headdim,
+                                   int64_t page_size, int64_t num_pages, int64_t bt_stride,
+                                   int64_t max_seqlen, int64_t causal, float scale,
+                                   void* workspace, size_t workspace_bytes, void* stream) {
+    return set_status(decode_impl(q, k_cache, v_cache, out, seq_lens, block_table, batch_size,
+                                  seqlen_q, num_heads, num_heads_k, headdim, page_size, num_pages,
+                                  bt_stride, max_seqlen, causal, scale, workspace,
+                                  workspace_bytes, static_cast<cudaStream_t>(stream), k_new,
+                                  v_new, seqlen_new));
+}
+
+extern "C" int pgqa_append_kv(const void* k_new, const void* v_new, void* k_cache,
+                              void* v_cache, const int32_t* seq_lens,
+                              const int32_t* block_table, int64_t batch_size, int64_t seqlen_new,
+                              int64_t num_heads_k, int64_t headdim, int64_t page_size,
+                              int64_t num_pages, int64_t bt_stride, void* workspace,
+                              void* stream) {
+    if (!k_new || !v_new || !k_cache || !v_cache || !seq_lens || !block_table)
+        return set_status(PGQA_ERR_NULL_POINTER);
+    if (batch_size <= 0 || seqlen_new < 0 || num_heads_k <= 0 || page_size <= 0 ||
+        num_pages <= 0 || bt_stride <= 0 || batch_size > INT32_MAX || seqlen_new > INT32_MAX ||
+        num_heads_k > INT32_MAX || page_size > INT32_MAX || num_pages > INT32_MAX ||
+        bt_stride > INT32_MAX)
+        return set_status(PGQA_ERR_BAD_SHAPE);
+    if (headdim != kHeadDim) return set_status(PGQA_ERR_UNSUPPORTED);
+    if ((reinterpret_cast<uintptr_t>(k_new) & 15) || (reinterpret_cast<uintptr_t>(v_new) & 15) ||
+        (reinterpret_cast<uintptr_t>(k_cache) & 15) || (reinterpret_cast<uintptr_t>(v_cache) & 15) ||
+        (reinterpret_cast<uintptr_t>(seq_lens) & 3) || (reinterpret_cast<uintptr_t>(block_table) & 3))
+        return set_status(PGQA_ERR_MISALIGNED);
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        cudaGetLastError();
+        return set_status(PGQA_ERR_NO_DEVICE);
+    }
+    DevInfo di;
+    int st = device_info(dev, &di);
+    if (st != PGQA_OK) return set_status(st);
+    if (workspace == nullptr) {
+        st = lib_workspace(dev, 256, &workspace);
+        if (st != PGQA_OK) return set_status(st);
+    }
+    AppendArgs a;
+    a.k_new = static_cast<const uint4*>(k_new);
+    a.v_new = static_cast<const uint4*>(v_new);
+    a.k_cache = static_cast<uint4*>(k_cache);
+    a.v_cache = static_cast<uint4*>(v_cache);
+    a.seq_lens = seq_lens;
+    a.block_table = block_table;
+    a.err = static_cast<int32_t*>(workspace);
+    a.B = (int32_t)batch_size;
+    a.S_new = (int32_t)seqlen_new;
+    a.Hkv = (int32_t)num_heads_k;
+    a.P = (int32_t)page_size;
+    a.bt_stride = (int32_t)bt_stride;
+    a.num_pages = (int32_t)num_pages;
+    a.cap_tokens = bt_stride * page_size;
+    if (launch_append(a, di.sms, static_cast<cudaStream_t>(stream)) != 0)
+        return set_status(PGQA_ERR_CUDA);
+    return set_status(PGQA_OK);
 }
 
 static size_t workspace_size_impl(int64_t batch_size, int64_t seqlen_q, int64_t num_heads,

@@ -7,7 +7,8 @@ task.md:33-54) with the same argument meaning: the block-table row width is
 num_blocks / batch_size, the pool has num_blocks pages and the scale is 1/sqrt(headdim).
 It launches on torch's current stream.
 
-`decode` is the general form (explicit scale, any pool size / table stride).
+`decode` is the general form (explicit scale, any pool size / table stride, several
+query tokens, optional append of new tokens); `append_kv` is the append step alone.
 
 Both run only the CUDA library: a missing or non-sm_100 device raises.
 """
@@ -60,13 +61,17 @@ def _check_tensors(q, k, v, out, seq_lens, block_table):
 
 
 def decode(q, k_cache, v_cache, block_table, seq_lens, scale=None, out=None,
-           max_seqlen=0, workspace=None, causal=False):
+           max_seqlen=0, workspace=None, causal=False, k_new=None, v_new=None):
     """Paged GQA decode.
 
     q [B, Hq, D] (one query token) or [B, Sq, Hq, D]; k_cache/v_cache
     [num_pages, P, Hkv, D] (bf16); block_table [B, stride] int32; seq_lens [B] int32.
-    With Sq > 1 and `causal`, query token i sees keys [0, L - Sq + i].  Returns out (same
-    shape as q).
+    With Sq > 1 and `causal`, query token i sees keys [0, L - Sq + i].
+
+    k_new / v_new [B, S_new, Hkv, D] (optional, as flash_attn_with_kvcache's k / v): the
+    new tokens are first written into the pools at positions [L_b, L_b + S_new) and the
+    decode then runs over L_b + S_new keys (seq_lens holds the lengths before the append
+    and is not modified).  Returns out (same shape as q).
     """
     if out is None:
         out = torch.empty_like(q)
@@ -79,18 +84,67 @@ def decode(q, k_cache, v_cache, block_table, seq_lens, scale=None, out=None,
         raise PgqaError(2, "decode: K/V pool shapes")
     if block_table.dim() != 2 or block_table.shape[0] != B or seq_lens.shape != (B,):
         raise PgqaError(2, "decode: block_table / seq_lens shapes")
+    S_new = _check_new_tokens(k_new, v_new, B, Hkv, D)
     if scale is None:
         scale = 1.0 / math.sqrt(D)
     if workspace is None:
         workspace = workspace_for(B, Hq, Hkv, D, P, q.device, seqlen_q=Sq)
     L = lib()
     with torch.cuda.device(q.device):
-        st = L.pgqa_decode_v2(_ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(out), _ptr(seq_lens),
-                              _ptr(block_table), B, Sq, Hq, Hkv, D, P, num_pages,
-                              block_table.stride(0), max_seqlen, int(bool(causal)), float(scale),
-                              _ptr(workspace), workspace.numel(), _stream_handle(q.device))
-    check(st, "pgqa_decode_v2")
+        if S_new == 0:
+            st = L.pgqa_decode_v2(_ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(out),
+                                  _ptr(seq_lens), _ptr(block_table), B, Sq, Hq, Hkv, D, P,
+                                  num_pages, block_table.stride(0), max_seqlen,
+                                  int(bool(causal)), float(scale), _ptr(workspace),
+                                  workspace.numel(), _stream_handle(q.device))
+            what = "pgqa_decode_v2"
+        else:
+            st = L.pgqa_decode_kvcache(_ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(k_new),
+                                       _ptr(v_new), _ptr(out), _ptr(seq_lens),
+                                       _ptr(block_table), B, Sq, S_new, Hq, Hkv, D, P,
+                                       num_pages, block_table.stride(0), max_seqlen,
+                                       int(bool(causal)), float(scale), _ptr(workspace),
+                                       workspace.numel(), _stream_handle(q.device))
+            what = "pgqa_decode_kvcache"
+    check(st, what)
     return out
+
+
+def _check_new_tokens(k_new, v_new, B, Hkv, D):
+    """Validates the appended tokens; returns S_new (0 when none are given)."""
+    if k_new is None and v_new is None:
+        return 0
+    if k_new is None or v_new is None:
+        raise ValueError("k_new and v_new go together")
+    for name, t in (("k_new", k_new), ("v_new", v_new)):
+        if not t.is_cuda or t.dtype != torch.bfloat16 or not t.is_contiguous():
+            raise ValueError(f"{name} must be a contiguous bf16 CUDA tensor")
+    if k_new.dim() != 4 or tuple(k_new.shape) != tuple(v_new.shape) or \
+            k_new.shape[0] != B or k_new.shape[2] != Hkv or k_new.shape[3] != D:
+        raise PgqaError(2, "k_new / v_new must be [B, S_new, Hkv, D]")
+    return k_new.shape[1]
+
+
+def append_kv(k_new, v_new, k_cache, v_cache, block_table, seq_lens, workspace=None):
+    """Write k_new / v_new [B, S_new, Hkv, D] into the pools at positions
+    [L_b, L_b + S_new) of each sequence (seq_lens = lengths before the append; not
+    modified).  Asynchronous on torch's current stream."""
+    for name, t, dt in (("k_cache", k_cache, torch.bfloat16), ("v_cache", v_cache, torch.bfloat16),
+                        ("seq_lens", seq_lens, torch.int32),
+                        ("block_table", block_table, torch.int32)):
+        if not t.is_cuda or t.dtype != dt or not t.is_contiguous():
+            raise ValueError(f"{name} must be a contiguous {dt} CUDA tensor")
+    num_pages, P, Hkv, D = k_cache.shape
+    B = block_table.shape[0]
+    S_new = _check_new_tokens(k_new, v_new, B, Hkv, D)
+    L = lib()
+    with torch.cuda.device(k_cache.device):
+        st = L.pgqa_append_kv(_ptr(k_new), _ptr(v_new), _ptr(k_cache), _ptr(v_cache),
+                              _ptr(seq_lens), _ptr(block_table), B, S_new, Hkv, D, P,
+                              num_pages, block_table.stride(0),
+                              _ptr(workspace) if workspace is not None else None,
+                              _stream_handle(k_cache.device))
+    check(st, "pgqa_append_kv")
 
 
 def run_kernel(q, k_cache_paged, v_cache_paged, output, cache_seqlens, block_table,

@@ -9,6 +9,7 @@ produced by the reference's own implementation of this path
 (submission_c500_regions.py:run_kernel, run on the CPU under the Triton interpreter by
 tests/golden/gen_golden.py).
 """
+from .append_kv import append_kv_ref  # noqa: F401
 from .paged_decode import (  # noqa: F401
     lse_combine_ref,
     paged_decode_ref,

@@ -98,3 +98,27 @@ def test_oracle_multi_query_restates_single_token():
         assert torch.allclose(causal[:, i], one, atol=1e-6)
     # L = 1 with 3 causal tokens: tokens 0 and 1 see nothing
     assert torch.count_nonzero(causal[0, :2]) == 0 and torch.count_nonzero(causal[0, 2]) > 0
+
+
+def test_append_oracle_places_tokens_after_each_sequence():
+    from mx_flash_attn_kernel_opt__b200 import inputs
+    from oracle import append_kv_ref
+    from oracle.paged_decode import _gather_seq
+    P, S_new = 16, 5
+    lens = [0, 11, 16, 40]
+    # the table covers the appended positions with distinct pages (the caller's job)
+    inp = inputs.custom_case(4, 8, 2, P, [L + S_new for L in lens], seed=8, width=4,
+                             spare_pages=3)
+    inp.seq_lens = torch.tensor(lens, dtype=torch.int32)
+    g = torch.Generator().manual_seed(9)
+    kn = torch.randn(4, S_new, 2, 128, generator=g).to(torch.bfloat16)
+    vn = torch.randn(4, S_new, 2, 128, generator=g).to(torch.bfloat16)
+    k2, v2 = append_kv_ref(inp.k, inp.v, kn, vn, inp.seq_lens, inp.block_table)
+    for b, L in enumerate(lens):
+        K0, V0 = _gather_seq(inp.k, inp.v, inp.block_table, b, L)
+        K1, V1 = _gather_seq(k2, v2, inp.block_table, b, L + S_new)
+        assert torch.equal(K1[:L], K0) and torch.equal(K1[L:], kn[b])
+        assert torch.equal(V1[:L], V0) and torch.equal(V1[L:], vn[b])
+    # nothing else changed
+    changed = (k2.view(torch.int16) != inp.k.view(torch.int16)).any(dim=(2, 3))
+    assert int(changed.sum()) <= 4 * S_new
