@@ -1,7 +1,7 @@
 """Benchmark of the paged-GQA decode on B200 (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--config c1..c5] [--no-e2e] [--no-cpu-baseline]
+                    [--config c1..c5] [--kv bf16|fp8] [--no-e2e] [--no-cpu-baseline]
 
 A step is one decode call over one batch of the workload.  Workload: config c2 (long
 context, B=2, Hq=64, Hkv=8, L=32768) at N=1; at N>1 (torchrun, one rank per GPU) config c5
@@ -18,6 +18,9 @@ roofline   achieved = algorithmic bytes per launch / mean launch time, against t
            HBM copy bandwidth in MEASURED_PEAKS.json; traffic from the committed ncu summary.
 cpu_baseline  the CPU oracle (fp32 PyTorch paged attention, all host threads) on a bounded
            sample of the same workload, rank 0 at N=1 only.
+
+--kv fp8 runs the same workload with e4m3 KV pages (per-KV-head scales; an extension,
+the reference's pools are bf16): value counts the e4m3 bytes; no e2e or CPU leg.
 
 --impl reference times that CPU implementation alone (the reference's path has no GPU
 implementation that runs on this machine).
@@ -54,6 +57,8 @@ def parse():
     ap.add_argument("--out", default=None, help="also append the JSON line to this file")
     ap.add_argument("--profile", type=int, default=0,
                     help="run N decode calls of the workload and exit (for ncu captures)")
+    ap.add_argument("--kv", default="bf16", choices=["bf16", "fp8"],
+                    help="KV page format: bf16 (the reference's) or e4m3 with per-head scales")
     return ap.parse_args()
 
 
@@ -263,13 +268,17 @@ def main():
     cfg = inputs.CONFIGS[name]
     lo, hi = sharding.kv_head_range(rank, world, cfg["Hkv"]) if world > 1 else (0, cfg["Hkv"])
     inp = inputs.baseline_config(name, device=dev, kv_head_range=(lo, hi))
+    fp8 = args.kv == "fp8"
+    if fp8:
+        inp = inputs.to_fp8(inp, keep_device=True)
+        torch.cuda.empty_cache()
     kv_bytes = inp.kv_bytes()
     alg_bytes = inp.algorithmic_bytes()
 
     # rotate input copies so the set read between two reuses is > 4x L2
     copies = max(1, math.ceil(4 * L2_BYTES / max(kv_bytes, 1)))
     free = torch.cuda.mem_get_info(dev)[0]
-    copies = max(1, min(copies, int(0.6 * free // max(2 * inp.k.numel() * 2, 1)) + 1, 64))
+    copies = max(1, min(copies, int(0.6 * free // max(2 * inp.k.numel() * inp.k.element_size(), 1)) + 1, 64))
     sets = [(inp.k, inp.v)]
     for _ in range(copies - 1):
         sets.append((inp.k.clone(), inp.v.clone()))
@@ -279,21 +288,31 @@ def main():
 
     # one correctness-checked call through the Python wrapper, then prebuilt C calls
     ops.decode(inp.q, inp.k, inp.v, inp.block_table, inp.seq_lens, scale=inp.scale, out=out,
-               workspace=ws)
+               workspace=ws, k_scale=inp.k_scale, v_scale=inp.v_scale)
     L = _lib.lib()
     vp = ctypes.c_void_p
     sh = vp(stream.cuda_stream)
-    argsets = [(vp(inp.q.data_ptr()), vp(k.data_ptr()), vp(v.data_ptr()), vp(out.data_ptr()),
-                vp(inp.seq_lens.data_ptr()), vp(inp.block_table.data_ptr()), inp.batch,
-                inp.num_heads, inp.num_heads_k, 128, inp.page_size, inp.num_pages,
-                inp.block_table.stride(0), 0, ctypes.c_float(inp.scale), vp(ws.data_ptr()),
-                ws.numel(), sh) for (k, v) in sets]
-    fn = L.pgqa_decode_v1
+    if fp8:
+        argsets = [(vp(inp.q.data_ptr()), vp(k.data_ptr()), vp(v.data_ptr()), None, None,
+                    vp(out.data_ptr()), vp(inp.seq_lens.data_ptr()),
+                    vp(inp.block_table.data_ptr()), inp.batch, 1, 0, inp.num_heads,
+                    inp.num_heads_k, 128, inp.page_size, inp.num_pages,
+                    inp.block_table.stride(0), 0, 0, ctypes.c_float(inp.scale),
+                    vp(inp.k_scale.data_ptr()), vp(inp.v_scale.data_ptr()), vp(ws.data_ptr()),
+                    ws.numel(), sh) for (k, v) in sets]
+        fn, fn_name = L.pgqa_decode_fp8, "pgqa_decode_fp8"
+    else:
+        argsets = [(vp(inp.q.data_ptr()), vp(k.data_ptr()), vp(v.data_ptr()), vp(out.data_ptr()),
+                    vp(inp.seq_lens.data_ptr()), vp(inp.block_table.data_ptr()), inp.batch,
+                    inp.num_heads, inp.num_heads_k, 128, inp.page_size, inp.num_pages,
+                    inp.block_table.stride(0), 0, ctypes.c_float(inp.scale), vp(ws.data_ptr()),
+                    ws.numel(), sh) for (k, v) in sets]
+        fn, fn_name = L.pgqa_decode_v1, "pgqa_decode_v1"
 
     def step(i):
         st = fn(*argsets[i % len(argsets)])
         if st != 0:
-            raise _lib.PgqaError(st, "pgqa_decode_v1")
+            raise _lib.PgqaError(st, fn_name)
 
     # warm-up: at least W steps and ~0.5 s (clock ramp-up, nvidia-smi samples)
     t_one = None
@@ -393,7 +412,7 @@ def main():
 
     # ---- end to end through the C symbol with host buffers ----
     e2e = None
-    if not args.no_e2e:
+    if not args.no_e2e and not fp8:
         e2e = e2e_measure(inp, dev, stream, steps, args.e2e_host_budget_gb, world)
         if world > 1:
             t = torch.tensor([e2e.pop("_ms"), e2e.pop("_kv")], dtype=torch.float64, device=dev)
@@ -407,7 +426,7 @@ def main():
             e2e["value"] = round(kvb / (ms / 1e3) / 1e9, 3)
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and not fp8:
         cpu = time_cpu_oracle(name, budget_s=10.0)
 
     if rank == 0:
@@ -416,9 +435,11 @@ def main():
             "steps": steps, "warmup": warm, "ms_per_step": el_ms_max / steps,
             "us_per_call": per_call_s * 1e6, "pct_of_peak": round(100 * value / world / peak, 2),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "bf16", "data": "synthetic",
+            "dtype": "e4m3 KV pages (per-KV-head fp32 scales), bf16 q/out, f16 MMA, fp32 softmax" if fp8 else "bf16",
+            "data": "synthetic",
             "config": {"workload": describe(name, world),
                        "kv_bytes_per_call": int(kv_total),
+                       "kv_format": args.kv,
                        "l2": (f"{len(sets)} rotating K/V pool copies, "
                               f"{len(sets) * kv_bytes / 1e6:.0f} MB read set per rank "
                               f"(> L2 {L2_BYTES / 1e6:.0f} MB)"),
@@ -427,7 +448,8 @@ def main():
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "peak_kind": f"{peak_kind} copy bandwidth (MEASURED_PEAKS.json hbm_gbs)",
                          "bytes_per_launch": int(alg_bytes),
-                         "traffic": committed_traffic(name if world == 1 else f"{name}/x{world}"),
+                         "traffic": committed_traffic((name if world == 1 else f"{name}/x{world}")
+                                                      + ("/fp8" if fp8 else "")),
                          "kernel": "pgqa_decode_kernel"},
             "gpu_launches": steps,
             "clocks": clocks,
@@ -456,14 +478,16 @@ def profile_calls(args, world):
     torch.cuda.set_device(dev)
     name = workload_for(args, world)
     inp = inputs.baseline_config(name, device=dev)
+    if args.kv == "fp8":
+        inp = inputs.to_fp8(inp, keep_device=True)
     out = torch.empty_like(inp.q)
     ws = ops.workspace_for(inp.batch, inp.num_heads, inp.num_heads_k, 128, inp.page_size, dev)
     for _ in range(args.profile):
         ops.decode(inp.q, inp.k, inp.v, inp.block_table, inp.seq_lens, scale=inp.scale, out=out,
-                   workspace=ws)
+                   workspace=ws, k_scale=inp.k_scale, v_scale=inp.v_scale)
     torch.cuda.synchronize(dev)
     ops.check_device_error(ws, dev)
-    print(json.dumps({"profile_calls": args.profile, "workload": name}))
+    print(json.dumps({"profile_calls": args.profile, "workload": name, "kv": args.kv}))
 
 
 def e2e_measure(inp, dev, stream, steps, budget_gb, world):

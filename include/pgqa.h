@@ -133,6 +133,31 @@ int pgqa_decode_kvcache(const void* q, void* k_cache, void* v_cache, const void*
                         size_t workspace_bytes, void* stream);
 
 /*
+ * FP8 KV pages (no counterpart in the reference, whose pools are bf16).  k_cache and
+ * v_cache hold float8 e4m3 (OCP "e4m3fn": bias 7, no infinities) in the same
+ * [num_pages, P, Hkv, D] layout, one byte per element; the value of an element of KV
+ * head h is e4m3 * k_scale[h] (resp. v_scale[h]) -- k_scale / v_scale are device arrays
+ * of Hkv floats, NULL meaning 1.  q and out stay bf16 [B, seqlen_q, Hq, D].  k_new /
+ * v_new (e4m3, [B, seqlen_new, Hkv, D], NULL when seqlen_new = 0) are appended first, as
+ * in pgqa_decode_kvcache.  Everything else is pgqa_decode_v2 / pgqa_decode_kvcache; the
+ * workspace size is pgqa_workspace_size_v2's.
+ */
+int pgqa_decode_fp8(const void* q, void* k_cache, void* v_cache, const void* k_new,
+                    const void* v_new, void* out, const int32_t* seq_lens,
+                    const int32_t* block_table, int64_t batch_size, int64_t seqlen_q,
+                    int64_t seqlen_new, int64_t num_heads, int64_t num_heads_k, int64_t headdim,
+                    int64_t page_size, int64_t num_pages, int64_t bt_stride, int64_t max_seqlen,
+                    int64_t causal, float scale, const float* k_scale, const float* v_scale,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
+/* pgqa_append_kv for e4m3 pools (128-byte token rows). */
+int pgqa_append_kv_fp8(const void* k_new, const void* v_new, void* k_cache, void* v_cache,
+                       const int32_t* seq_lens, const int32_t* block_table, int64_t batch_size,
+                       int64_t seqlen_new, int64_t num_heads_k, int64_t headdim,
+                       int64_t page_size, int64_t num_pages, int64_t bt_stride, void* workspace,
+                       void* stream);
+
+/*
  * Allocation-free variant of pgqa_decode_v1 (no counterpart in the reference).
  *
  * Some callers cannot allocate device memory when they call the decode: code running

@@ -45,6 +45,9 @@ SIGNATURES = {
     "pgqa_append_kv": (ctypes.c_int, [c_void_p] * 6 + [c_int64] * 7 + [c_void_p] * 2),
     "pgqa_decode_kvcache": (ctypes.c_int, [c_void_p] * 8 + [c_int64] * 11 +
                             [c_float, c_void_p, c_size_t, c_void_p]),
+    "pgqa_append_kv_fp8": (ctypes.c_int, [c_void_p] * 6 + [c_int64] * 7 + [c_void_p] * 2),
+    "pgqa_decode_fp8": (ctypes.c_int, [c_void_p] * 8 + [c_int64] * 11 +
+                        [c_float, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
     "pgqa_workspace_size": (c_size_t, [c_int64] * 5),
     "pgqa_workspace_init": (ctypes.c_int, [c_void_p, c_size_t, c_void_p]),
     "pgqa_last_status": (ctypes.c_int, []),

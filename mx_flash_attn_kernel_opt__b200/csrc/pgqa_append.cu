@@ -7,12 +7,13 @@
  * with k = v = None) -- writes k/v [B, S_new, Hkv, D] at token positions
  * [L_b, L_b + S_new) of sequence b (L_b = cache_seqlens[b], the length before the
  * append) and then attends over L_b + S_new keys.  Token t of sequence b lives in slot
- * t % P of page block_table[b, t / P] (task.md:94,146), one 256-byte row per KV head.
+ * t % P of page block_table[b, t / P] (task.md:94,146), one row per KV head.
  *
- * The step is a scatter of 256-byte rows: each thread moves one 16-byte piece of K and
- * the same piece of V, so a warp writes two complete rows (coalesced 256-byte runs) and
- * reads k/v in their contiguous order.  It launches as a programmatic dependent and
- * waits (griddepcontrol.wait) before touching memory, so it may overlap the previous
+ * The step is a scatter of token rows (256 bytes for bf16 pools, 128 for e4m3): each
+ * thread moves one 16-byte piece of K and the same piece of V, so a warp writes whole
+ * rows (coalesced runs) and reads k/v in their contiguous order.  It launches as a
+ * programmatic dependent and waits (griddepcontrol.wait) before touching memory, so it
+ * may overlap the previous
  * kernel's tail without racing its reads of the pool.  Rows whose position lies past
  * the table's capacity, or whose page id is outside [0, num_pages), are skipped and
  * flagged in the device error word.
@@ -28,17 +29,17 @@ namespace pgqa {
 namespace {
 
 constexpr int kAppendThreads = 256;
-constexpr int kPiecesPerRow = 16;  // 128 bf16 = 256 B = 16 x 16 B
 
 __global__ void __launch_bounds__(kAppendThreads)
 append_kv_kernel(const AppendArgs a) {
     ptx::griddep_wait();
-    const int64_t total = (int64_t)a.B * a.S_new * a.Hkv * kPiecesPerRow;
+    const int sh = a.row_pieces_log2;
+    const int64_t total = ((int64_t)a.B * a.S_new * a.Hkv) << sh;
     const int64_t stride = (int64_t)gridDim.x * kAppendThreads;
     int32_t bad = 0;
     for (int64_t x = (int64_t)blockIdx.x * kAppendThreads + threadIdx.x; x < total; x += stride) {
-        const int64_t row = x >> 4;               // (b, s, kvh) row of k_new / v_new
-        const int piece = (int)(x & 15);
+        const int64_t row = x >> sh;              // (b, s, kvh) row of k_new / v_new
+        const int piece = (int)(x & ((1 << sh) - 1));
         const int32_t kvh = (int32_t)(row % a.Hkv);
         const int64_t bs = row / a.Hkv;
         const int32_t s = (int32_t)(bs % a.S_new);
@@ -48,7 +49,7 @@ append_kv_kernel(const AppendArgs a) {
         if (L0 < 0 || t >= a.cap_tokens) { bad |= kAppendBadSeqlen; continue; }
         const int32_t pid = __ldg(a.block_table + (int64_t)b * a.bt_stride + t / a.P);
         if (pid < 0 || pid >= a.num_pages) { bad |= kAppendBadPage; continue; }
-        const int64_t dst = (((int64_t)pid * a.P + t % a.P) * a.Hkv + kvh) * kPiecesPerRow + piece;
+        const int64_t dst = ((((int64_t)pid * a.P + t % a.P) * a.Hkv + kvh) << sh) + piece;
         const uint4 kv = __ldg(a.k_new + x);
         const uint4 vv = __ldg(a.v_new + x);
         a.k_cache[dst] = kv;
@@ -60,7 +61,7 @@ append_kv_kernel(const AppendArgs a) {
 }  // namespace
 
 int launch_append(const AppendArgs& a, int num_sms, cudaStream_t stream) {
-    const int64_t total = (int64_t)a.B * a.S_new * a.Hkv * kPiecesPerRow;
+    const int64_t total = ((int64_t)a.B * a.S_new * a.Hkv) << a.row_pieces_log2;
     if (total == 0) return 0;
     int64_t blocks = (total + kAppendThreads - 1) / kAppendThreads;
     const int64_t cap = (int64_t)num_sms * 8;  // 8 resident 256-thread CTAs per SM

@@ -41,6 +41,7 @@
 #include <math.h>
 #include <stddef.h>
 #include <mutex>
+#include <type_traits>
 
 #include "../../include/pgqa.h"
 #include "pgqa_append.h"
@@ -55,6 +56,8 @@ namespace pgqa {
 
 constexpr int kStageBytes = 8192;          // K (2 x 2 KB halves) + V (2 x 2 KB halves)
 constexpr int kHalfBytes = 2048;           // 16 tokens x 64 dims x bf16
+constexpr int kStageBytesKv8 = 4096;       // FP8 pools: K (16 tokens x 128 B) + V
+constexpr float kLazyLog2 = 8.f;           // softmax reference max moves only beyond 2^8
 constexpr uint64_t kWaitLimitNs = 1000000000ull;  // 1 s bound on any single wait
 
 enum DeviceErr : int32_t { kErrTimeout = 1, kErrBadPage = 2, kErrBadSeqlen = 4 };
@@ -75,6 +78,8 @@ struct DecodeParams {
     int32_t rows;    // query rows per KV head = g * Sq (row r: head r / Sq, token r % Sq)
     int32_t causal;  // query token i sees keys [0, L - Sq + i] instead of [0, L)
     int32_t len_add; // tokens appended by this call: sequence b has seq_lens[b] + len_add keys
+    const float* k_scale;  // FP8 pools: dequantisation factor per KV head (null = 1)
+    const float* v_scale;
     int32_t page_size, bt_stride, num_pages;
     int64_t cap_tokens;  // bt_stride * page_size (clamp for seq_lens)
     float scale_log2;    // scale * log2(e)
@@ -159,6 +164,28 @@ __device__ __forceinline__ void store_out_tile(__nv_bfloat16* head_row, float f0
     }
 }
 
+/* FP8 pools: the PV accumulator rows of M tile u map to d = 16u + 2*gid (row gid) and
+ * 16u + 2*gid + 1 (row gid + 8), the order in which the transposed byte-pair loads
+ * deliver V.  After the transposes a lane holds d = 16u + 4*tig + {0, 2} (y0) and
+ * {1, 3} (y1) of head gid; interleave and store 4 consecutive values. */
+__device__ __forceinline__ void store_out_tile_kv8(__nv_bfloat16* head_row, float f0, float f1,
+                                                   float f2, float f3, float sA, float sB, int u,
+                                                   int tig, bool valid) {
+    const uint32_t y0 = ptx::movmatrix_t(ptx::pack_bf16x2(f0 * sA, f1 * sB));
+    const uint32_t y1 = ptx::movmatrix_t(ptx::pack_bf16x2(f2 * sA, f3 * sB));
+    if (valid)
+        *reinterpret_cast<uint2*>(head_row + u * 16 + 4 * tig) =
+            make_uint2(ptx::prmt(y0, y1, 0x5410u), ptx::prmt(y0, y1, 0x7632u));
+}
+
+template <bool KV8>
+__device__ __forceinline__ void store_tile(__nv_bfloat16* head_row, float f0, float f1, float f2,
+                                           float f3, float sA, float sB, int mt, int tig,
+                                           bool valid) {
+    if (KV8) store_out_tile_kv8(head_row, f0, f1, f2, f3, sA, sB, mt, tig, valid);
+    else store_out_tile(head_row, f0, f1, f2, f3, sA, sB, mt, tig, valid);
+}
+
 /* Query row r (of the Hq/Hkv * Sq rows of KV head kvh) of sequence b: head kvh*g + r/Sq,
  * token r%Sq.  Returns its offset (in elements) in q / out, whose layout is
  * [B, Sq, Hq, 128]. */
@@ -214,17 +241,23 @@ struct PairMerge {
 
 /* MQ = false: one query token per sequence (rows = heads, every row sees [0, L)); the
  * per-row masks and empty-row guards compile away.  MQ = true: seqlen_q tokens, optional
- * causal limits per row. */
-template <int W, int S, bool MQ>
+ * causal limits per row.
+ * KV8 = false: bf16 pools, 8 KB stages (K and V as two 64-dim boxes each), bf16 MMAs.
+ * KV8 = true: e4m3 pools, 4 KB stages (one 128-byte box each for K and V); the fp8
+ * bytes are converted exactly to f16 after ldmatrix and multiplied with f16 MMAs
+ * (q rounded to f16 after an exact per-row power-of-two rescale; P in f16). */
+template <int W, int S, bool MQ, bool KV8>
 __global__ void __launch_bounds__(W * 32, 1)
 pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
                    const __grid_constant__ CUtensorMap vmap, const DecodeParams p) {
     constexpr int NT = W * 32;
+    constexpr int kStage = KV8 ? kStageBytesKv8 : kStageBytes;
+    constexpr int kVOff = KV8 ? kHalfBytes : 2 * kHalfBytes;  // V's offset inside a stage
     extern __shared__ uint8_t smem_raw[];
     // 128-byte TMA swizzle needs 1024-byte aligned stages (shared-window offset).
     uint8_t* smem = smem_raw + ((1024u - (ptx::smem_u32(smem_raw) & 1023u)) & 1023u);
-    uint8_t* ring = smem;                                                  // W*S*8 KB
-    uint64_t* bars = reinterpret_cast<uint64_t*>(ring + W * S * kStageBytes);  // W*S
+    uint8_t* ring = smem;                                                  // W*S stages
+    uint64_t* bars = reinterpret_cast<uint64_t*>(ring + W * S * kStage);   // W*S
     int32_t* misc = reinterpret_cast<int32_t*>(bars + W * S);               // 64 ints
     uint32_t* pre = reinterpret_cast<uint32_t*>(misc + 64);                 // B+1
 
@@ -321,11 +354,14 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
         int32_t win_b = -1, win_p0 = 0, win_pid = 0;
         int64_t issued = 0;
         const int P = p.page_size;
+        // page / slot of the issue cursor's chunk and its KV head, stepped with the cursor
+        // (no division per chunk: chunks are 16-token aligned and P is a multiple of 16)
+        int32_t ipage = (ic.c * kChunkTokens) / P;
+        int32_t ioff = ic.c * kChunkTokens - ipage * P;
+        int32_t ikvh = ic.j / p.n_hg;
 
         auto issue_next = [&]() {
-            const int32_t tok = ic.c * kChunkTokens;
-            const int32_t page = tok / P;
-            const int32_t off = tok - page * P;
+            const int32_t page = ipage;
             if (ic.b != win_b || page < win_p0 || page >= win_p0 + 32) {
                 win_b = ic.b;
                 win_p0 = page;
@@ -341,19 +377,34 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
                 }
                 const int stage = (int)(issued % S);
                 const uint32_t bar = bar_base + (uint32_t)(warp * S + stage) * 8u;
-                const uint32_t dst = ring_base + (uint32_t)(warp * S + stage) * kStageBytes;
-                const int32_t kvh = ic.j / p.n_hg;
-                const int32_t z = pid * P + off;
+                const uint32_t dst = ring_base + (uint32_t)(warp * S + stage) * kStage;
+                const int32_t kvh = ikvh;
+                const int32_t z = pid * P + ioff;
                 const uint32_t extra =
                     (p.debug_stuck && blockIdx.x == 0 && warp == 0 && issued == 0) ? 16u : 0u;
-                ptx::mbar_arrive_expect_tx(bar, kStageBytes + extra);
-                ptx::tma_load_3d(dst, &kmap, bar, 0, kvh, z, pol);
-                ptx::tma_load_3d(dst + kHalfBytes, &kmap, bar, 64, kvh, z, pol);
-                ptx::tma_load_3d(dst + 2 * kHalfBytes, &vmap, bar, 0, kvh, z, pol);
-                ptx::tma_load_3d(dst + 3 * kHalfBytes, &vmap, bar, 64, kvh, z, pol);
+                ptx::mbar_arrive_expect_tx(bar, kStage + extra);
+                if (KV8) {
+                    ptx::tma_load_3d(dst, &kmap, bar, 0, kvh, z, pol);
+                    ptx::tma_load_3d(dst + kVOff, &vmap, bar, 0, kvh, z, pol);
+                } else {
+                    ptx::tma_load_3d(dst, &kmap, bar, 0, kvh, z, pol);
+                    ptx::tma_load_3d(dst + kHalfBytes, &kmap, bar, 64, kvh, z, pol);
+                    ptx::tma_load_3d(dst + 2 * kHalfBytes, &vmap, bar, 0, kvh, z, pol);
+                    ptx::tma_load_3d(dst + 3 * kHalfBytes, &vmap, bar, 64, kvh, z, pol);
+                }
             }
             ++issued;
-            if (issued < ntot) advance(p, pre, ic);
+            if (issued < ntot) {
+                advance(p, pre, ic);
+                if (ic.c == 0) {  // a new unit starts at its first chunk
+                    ipage = 0;
+                    ioff = 0;
+                    ikvh = (p.n_hg == 1) ? ic.j : ic.j / p.n_hg;
+                } else if ((ioff += kChunkTokens) == P) {
+                    ioff = 0;
+                    ++ipage;
+                }
+            }
         };
 
         const int64_t prologue = ntot < S ? ntot : S;
@@ -362,13 +413,51 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
         uint32_t qf[16];
         int nh_valid = 0;
         int32_t limA = 0, limB = 0;  // keys visible to this lane's two columns (rows)
+        // score multipliers of this lane's two columns and the V factor (FP8 pools)
+        float mulA = p.scale_log2, mulB = p.scale_log2, vsc = 1.f;
         auto load_q = [&](const Cursor& cu) {
             const int32_t kvh = cu.j / p.n_hg;
             const int32_t hg = cu.j - kvh * p.n_hg;
             nh_valid = min(kHeadsPerGroup, p.rows - hg * kHeadsPerGroup);
             limA = row_limit<MQ>(p, hg * kHeadsPerGroup + 2 * tig, cu.L);
             limB = row_limit<MQ>(p, hg * kHeadsPerGroup + 2 * tig + 1, cu.L);
-            if (gid < nh_valid) {
+            if (KV8) {
+                /* qf[4m + 2hh + j] = f16 pair q[32m + 16hh + 4tig + 2j + {0,1}] of row gid,
+                 * the d order of the converted K fragments.  The row is scaled by 2^e
+                 * (exact) so that its largest |q| lies in [2^14, 2^15): f16 then keeps all
+                 * of bf16's precision without overflow; 2^-e goes into the score
+                 * multiplier of that column. */
+                float qv[32];
+                if (gid < nh_valid) {
+                    const __nv_bfloat16* qp = p.q + row_offset<MQ>(p, cu.b, kvh, hg * kHeadsPerGroup + gid);
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) {
+                        const uint2 w = __ldg(reinterpret_cast<const uint2*>(qp + 16 * k + 4 * tig));
+                        const float2 f0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.x));
+                        const float2 f1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.y));
+                        qv[4 * k] = f0.x; qv[4 * k + 1] = f0.y; qv[4 * k + 2] = f1.x; qv[4 * k + 3] = f1.y;
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) qv[i] = 0.f;
+                }
+                float mx = 0.f;
+#pragma unroll
+                for (int i = 0; i < 32; ++i) mx = fmaxf(mx, fabsf(qv[i]));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+                int e = 0;
+                if (mx > 0.f) e = 14 - ((int)((__float_as_uint(mx) >> 23) & 0xff) - 127);
+                e = max(-126, min(60, e));
+                const float up = __uint_as_float((uint32_t)(e + 127) << 23);
+                const float down = __uint_as_float((uint32_t)(127 - e) << 23);
+#pragma unroll
+                for (int i = 0; i < 16; ++i) qf[i] = ptx::pack_f16x2(qv[2 * i] * up, qv[2 * i + 1] * up);
+                const float ks = p.k_scale ? __ldg(p.k_scale + kvh) : 1.f;
+                vsc = p.v_scale ? __ldg(p.v_scale + kvh) : 1.f;
+                mulA = p.scale_log2 * ks * __shfl_sync(0xffffffffu, down, 8 * tig);
+                mulB = p.scale_log2 * ks * __shfl_sync(0xffffffffu, down, 8 * tig + 4);
+            } else if (gid < nh_valid) {
                 const uint32_t* qp = reinterpret_cast<const uint32_t*>(
                     p.q + row_offset<MQ>(p, cu.b, kvh, hg * kHeadsPerGroup + gid));
 #pragma unroll
@@ -400,116 +489,201 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
         const int tK = mr + 8 * (mj & 1);
         const int tV = mr + 8 * (mj >> 1);
 
-        for (int64_t i = 0; i < ntot; ++i) {
-            const int stage = (int)(i % S);
-            const uint32_t bar = bar_base + (uint32_t)(warp * S + stage) * 8u;
-            if (!ptx::wait_parity_bounded(bar, (uint32_t)((i / S) & 1), p.wait_limit_ns)) {
-                if (lane == 0) atomicOr(p.err, kErrTimeout);
-                aborted = true;
-                // Drain: wait (bounded) for every copy still in flight into this ring.
-                for (int64_t k = i; k < issued; ++k) {
-                    const uint32_t b2 = bar_base + (uint32_t)(warp * S + (int)(k % S)) * 8u;
-                    ptx::wait_parity_bounded(b2, (uint32_t)((k / S) & 1), p.wait_limit_ns);
+        /* One step streams NC = 1 chunk, or NC = 2 consecutive chunks of the same unit
+         * (FP8 pools: two independent QK chains and one softmax vote per 32 tokens; the
+         * 4-stage ring keeps two more chunks in flight meanwhile).  Returns false when a
+         * wait expired (the ring is drained and the warp stops). */
+        constexpr bool kPair = KV8;
+        int64_t i = 0;
+        auto step = [&](auto nc_tag) -> bool {
+            constexpr int NC = decltype(nc_tag)::value;
+#pragma unroll
+            for (int c = 0; c < NC; ++c) {
+                const int64_t k = i + c;
+                const uint32_t bar = bar_base + (uint32_t)(warp * S + (int)(k % S)) * 8u;
+                if (!ptx::wait_parity_bounded(bar, (uint32_t)((k / S) & 1), p.wait_limit_ns)) {
+                    if (lane == 0) atomicOr(p.err, kErrTimeout);
+                    aborted = true;
+                    // Drain: wait (bounded) for every copy still in flight into this ring.
+                    for (int64_t k2 = k; k2 < issued; ++k2) {
+                        const uint32_t b2 = bar_base + (uint32_t)(warp * S + (int)(k2 % S)) * 8u;
+                        ptx::wait_parity_bounded(b2, (uint32_t)((k2 / S) & 1), p.wait_limit_ns);
+                    }
+                    return false;
                 }
-                break;
             }
-            const uint32_t sK = ring_base + (uint32_t)(warp * S + stage) * kStageBytes;
-            const uint32_t sV = sK + 2 * kHalfBytes;
-
-            const bool last_of_unit = (cc.c == cc.n - 1);
-            const int nvalid = last_of_unit ? (cc.L - cc.c * kChunkTokens) : kChunkTokens;
+            // only the step's last chunk can be the last of its unit
+            const bool last_of_unit = (cc.c + NC - 1 == cc.n - 1);
+            const int nvalid = last_of_unit ? (cc.L - (cc.c + NC - 1) * kChunkTokens) : kChunkTokens;
             if (nvalid < kChunkTokens) {
                 /* Tokens past the sequence end inside the last page: zero their V rows so
                  * that p = 0 never meets a non-finite V value (0 * NaN). */
-                uint8_t* vrow = ring + (size_t)(warp * S + stage) * kStageBytes + 2 * kHalfBytes;
-                const int units = (kChunkTokens - nvalid) * 16;  // 16-byte pieces, both halves
-                for (int u = lane; u < units; u += 32) {
-                    const int t = nvalid + (u >> 4);
-                    const int half = (u >> 3) & 1;
-                    const int c16 = u & 7;
-                    *reinterpret_cast<uint4*>(vrow + half * kHalfBytes + t * 128 + c16 * 16) =
-                        make_uint4(0, 0, 0, 0);
+                const int64_t k = i + NC - 1;
+                uint8_t* vrow = ring + (size_t)(warp * S + (int)(k % S)) * kStage + kVOff;
+                if (KV8) {
+                    const int units = (kChunkTokens - nvalid) * 8;  // 16-byte pieces of 128-B rows
+                    for (int u = lane; u < units; u += 32)
+                        *reinterpret_cast<uint4*>(vrow + (nvalid + (u >> 3)) * 128 + (u & 7) * 16) =
+                            make_uint4(0, 0, 0, 0);
+                } else {
+                    const int units = (kChunkTokens - nvalid) * 16;  // 16-byte pieces, both halves
+                    for (int u = lane; u < units; u += 32) {
+                        const int t = nvalid + (u >> 4);
+                        const int half = (u >> 3) & 1;
+                        const int c16 = u & 7;
+                        *reinterpret_cast<uint4*>(vrow + half * kHalfBytes + t * 128 + c16 * 16) =
+                            make_uint4(0, 0, 0, 0);
+                    }
                 }
                 ptx::fence_proxy_async_smem();  // before TMA overwrites this stage again
                 __syncwarp();
             }
 
-            /* ---- S^T = K . Q^T : 16 tokens x 8 heads, K-dim = 128 ---- */
-            float sa[4] = {0.f, 0.f, 0.f, 0.f};
-            float sb[4] = {0.f, 0.f, 0.f, 0.f};
+            /* ---- S^T = K . Q^T : 16 tokens x 8 heads per chunk, K-dim = 128 ----
+             * s[c][0]: (t=gid, h=2tig) [1]: (gid, 2tig+1) [2]: (gid+8, 2tig) [3]: (gid+8, 2tig+1) */
+            float s[NC][4];
 #pragma unroll
-            for (int ks = 0; ks < 8; ++ks) {
-                const int half = ks >> 2;
-                const int ch = ((2 * ks) + (mj >> 1)) & 7;
-                const uint32_t addr = sK + half * kHalfBytes + tK * 128 + ((ch ^ mr) << 4);
-                uint32_t a0, a1, a2, a3;
-                ptx::ldsm_x4(addr, a0, a1, a2, a3);
-                if (ks & 1) ptx::mma_bf16_16816(sb, a0, a1, a2, a3, qf[2 * ks], qf[2 * ks + 1]);
-                else        ptx::mma_bf16_16816(sa, a0, a1, a2, a3, qf[2 * ks], qf[2 * ks + 1]);
-            }
-            // s[0]: (t=gid, h=2tig) s[1]: (gid, 2tig+1) s[2]: (gid+8, 2tig) s[3]: (gid+8, 2tig+1)
-            float s[4];
+            for (int c = 0; c < NC; ++c) {
+                const uint32_t sK = ring_base + (uint32_t)(warp * S + (int)((i + c) % S)) * kStage;
+                float sa[4] = {0.f, 0.f, 0.f, 0.f};
+                float sb[4] = {0.f, 0.f, 0.f, 0.f};
+                if (KV8) {
+                    /* One ldmatrix.x4 per 32 dims: matrices (t 0-7 | 8-15) x (16-byte units
+                     * 2m | 2m+1); a lane gets 4 consecutive fp8 of one token, which convert
+                     * exactly into the A fragments of two k16 f16 MMAs (k slot 2tig+j <-> d
+                     * 4tig+j, 2tig+8+j <-> 4tig+2+j, matched by qf's order).  (e4m3 MMAs on
+                     * the stored bytes, with q split in two e4m3 parts, measured slower.) */
 #pragma unroll
-            for (int r = 0; r < 4; ++r) s[r] = (sa[r] + sb[r]) * p.scale_log2;
-            if (MQ) {
-                // keys past the row's limit (the sequence end, or the causal bound) -> -inf
-                const int32_t t = cc.c * kChunkTokens + gid;
-                s[0] = (t < limA) ? s[0] : -INFINITY;
-                s[1] = (t < limB) ? s[1] : -INFINITY;
-                s[2] = (t + 8 < limA) ? s[2] : -INFINITY;
-                s[3] = (t + 8 < limB) ? s[3] : -INFINITY;
-            } else if (nvalid < kChunkTokens) {
-                // tokens past the sequence end -> -inf (every row sees the same keys)
-                if (gid >= nvalid) { s[0] = -INFINITY; s[1] = -INFINITY; }
-                if (gid + 8 >= nvalid) { s[2] = -INFINITY; s[3] = -INFINITY; }
+                    for (int m = 0; m < 4; ++m) {
+                        const int u = 2 * m + (mj >> 1);
+                        const uint32_t addr = sK + tK * 128 + ((u ^ mr) << 4);
+                        uint32_t r0, r1, r2, r3;
+                        ptx::ldsm_x4(addr, r0, r1, r2, r3);
+                        uint32_t k0l, k0h, k1l, k1h, k2l, k2h, k3l, k3h;
+                        ptx::e4m3x4_to_f16(r0, k0l, k0h);
+                        ptx::e4m3x4_to_f16(r1, k1l, k1h);
+                        ptx::e4m3x4_to_f16(r2, k2l, k2h);
+                        ptx::e4m3x4_to_f16(r3, k3l, k3h);
+                        ptx::mma_f16_16816(sa, k0l, k1l, k0h, k1h, qf[4 * m], qf[4 * m + 1]);
+                        ptx::mma_f16_16816(sb, k2l, k3l, k2h, k3h, qf[4 * m + 2], qf[4 * m + 3]);
+                    }
+                    s[c][0] = (sa[0] + sb[0]) * mulA; s[c][1] = (sa[1] + sb[1]) * mulB;
+                    s[c][2] = (sa[2] + sb[2]) * mulA; s[c][3] = (sa[3] + sb[3]) * mulB;
+                } else {
+#pragma unroll
+                    for (int ks = 0; ks < 8; ++ks) {
+                        const int half = ks >> 2;
+                        const int ch = ((2 * ks) + (mj >> 1)) & 7;
+                        const uint32_t addr = sK + half * kHalfBytes + tK * 128 + ((ch ^ mr) << 4);
+                        uint32_t a0, a1, a2, a3;
+                        ptx::ldsm_x4(addr, a0, a1, a2, a3);
+                        if (ks & 1) ptx::mma_bf16_16816(sb, a0, a1, a2, a3, qf[2 * ks], qf[2 * ks + 1]);
+                        else        ptx::mma_bf16_16816(sa, a0, a1, a2, a3, qf[2 * ks], qf[2 * ks + 1]);
+                    }
+#pragma unroll
+                    for (int r = 0; r < 4; ++r) s[c][r] = (sa[r] + sb[r]) * p.scale_log2;
+                }
+                if (MQ) {
+                    // keys past the row's limit (the sequence end, or the causal bound) -> -inf
+                    const int32_t t = (cc.c + c) * kChunkTokens + gid;
+                    s[c][0] = (t < limA) ? s[c][0] : -INFINITY;
+                    s[c][1] = (t < limB) ? s[c][1] : -INFINITY;
+                    s[c][2] = (t + 8 < limA) ? s[c][2] : -INFINITY;
+                    s[c][3] = (t + 8 < limB) ? s[c][3] : -INFINITY;
+                } else if (c == NC - 1 && nvalid < kChunkTokens) {
+                    // tokens past the sequence end -> -inf (every row sees the same keys)
+                    if (gid >= nvalid) { s[c][0] = -INFINITY; s[c][1] = -INFINITY; }
+                    if (gid + 8 >= nvalid) { s[c][2] = -INFINITY; s[c][3] = -INFINITY; }
+                }
             }
 
-            /* ---- online softmax (log2 domain), heads hA = 2tig, hB = 2tig+1 ---- */
-            float mxA = fmaxf(s[0], s[2]);
-            float mxB = fmaxf(s[1], s[3]);
+            /* ---- online softmax (log2 domain), heads hA = 2tig, hB = 2tig+1 ----
+             * Lazy rescale: the reference max m2 of a column moves only when one of its
+             * scores exceeds it by more than kLazyLog2, so p <= 2^kLazyLog2 (fine in f16 /
+             * bf16 and fp32).  o and l share the reference, so the result is the same; the
+             * column reduction and the rescale of o and l run only when a lane votes. */
+            float mxA = fmaxf(s[0][0], s[0][2]);
+            float mxB = fmaxf(s[0][1], s[0][3]);
 #pragma unroll
-            for (int off = 4; off < 32; off <<= 1) {
-                mxA = fmaxf(mxA, __shfl_xor_sync(0xffffffffu, mxA, off));
-                mxB = fmaxf(mxB, __shfl_xor_sync(0xffffffffu, mxB, off));
+            for (int c = 1; c < NC; ++c) {
+                mxA = fmaxf(mxA, fmaxf(s[c][0], s[c][2]));
+                mxB = fmaxf(mxB, fmaxf(s[c][1], s[c][3]));
             }
-            const float mnA = fmaxf(m2[0], mxA);
-            const float mnB = fmaxf(m2[1], mxB);
-            // a row with no visible key yet keeps max -inf: exponentiate against 0 instead
+            if (__any_sync(0xffffffffu, mxA > m2[0] + kLazyLog2 || mxB > m2[1] + kLazyLog2)) {
+#pragma unroll
+                for (int off = 4; off < 32; off <<= 1) {
+                    mxA = fmaxf(mxA, __shfl_xor_sync(0xffffffffu, mxA, off));
+                    mxB = fmaxf(mxB, __shfl_xor_sync(0xffffffffu, mxB, off));
+                }
+                const float mnA = fmaxf(m2[0], mxA);
+                const float mnB = fmaxf(m2[1], mxB);
+                // a row with no visible key yet keeps max -inf: rescale against 0 instead
+                const float zA = (MQ && mnA == -INFINITY) ? 0.f : mnA;
+                const float zB = (MQ && mnB == -INFINITY) ? 0.f : mnB;
+                const float alA = ptx::ex2(m2[0] - zA);
+                const float alB = ptx::ex2(m2[1] - zB);
+                m2[0] = mnA;
+                m2[1] = mnB;
+                l2[0] *= alA;
+                l2[1] *= alB;
+#pragma unroll
+                for (int mt = 0; mt < 8; ++mt) {
+                    o[mt][0] *= alA; o[mt][1] *= alB; o[mt][2] *= alA; o[mt][3] *= alB;
+                }
+            }
             // (with one query token every chunk holds a visible key for every row)
-            const float bsA = (MQ && mnA == -INFINITY) ? 0.f : mnA;
-            const float bsB = (MQ && mnB == -INFINITY) ? 0.f : mnB;
-            const float alA = ptx::ex2(m2[0] - bsA);
-            const float alB = ptx::ex2(m2[1] - bsB);
-            m2[0] = mnA;
-            m2[1] = mnB;
-            const float p0 = ptx::ex2(s[0] - bsA);
-            const float p1 = ptx::ex2(s[1] - bsB);
-            const float p2 = ptx::ex2(s[2] - bsA);
-            const float p3 = ptx::ex2(s[3] - bsB);
-            l2[0] = fmaf(l2[0], alA, p0 + p2);
-            l2[1] = fmaf(l2[1], alB, p1 + p3);
+            const float bsA = (MQ && m2[0] == -INFINITY) ? 0.f : m2[0];
+            const float bsB = (MQ && m2[1] == -INFINITY) ? 0.f : m2[1];
 #pragma unroll
-            for (int mt = 0; mt < 8; ++mt) {
-                o[mt][0] *= alA; o[mt][1] *= alB; o[mt][2] *= alA; o[mt][3] *= alB;
-            }
-            /* P^T (tokens x heads) C-fragment -> B-fragment of the PV MMA. */
-            const uint32_t pb0 = ptx::movmatrix_t(ptx::pack_bf16x2(p0, p1));
-            const uint32_t pb1 = ptx::movmatrix_t(ptx::pack_bf16x2(p2, p3));
+            for (int c = 0; c < NC; ++c) {
+                const float p0 = ptx::ex2(s[c][0] - bsA);
+                const float p1 = ptx::ex2(s[c][1] - bsB);
+                const float p2 = ptx::ex2(s[c][2] - bsA);
+                const float p3 = ptx::ex2(s[c][3] - bsB);
+                l2[0] += p0 + p2;
+                l2[1] += p1 + p3;
+                /* P^T (tokens x heads) C-fragment -> B-fragment of the PV MMA. */
+                const uint32_t pb0 = ptx::movmatrix_t(KV8 ? ptx::pack_f16x2(p0, p1) : ptx::pack_bf16x2(p0, p1));
+                const uint32_t pb1 = ptx::movmatrix_t(KV8 ? ptx::pack_f16x2(p2, p3) : ptx::pack_bf16x2(p2, p3));
 
-            /* ---- O^T += V^T . P^T : 128 dims (8 M tiles) x 8 heads, K-dim = 16 tokens ---- */
+                /* ---- O^T += V^T . P^T : 128 dims (8 M tiles) x 8 heads, K-dim = 16 tokens ---- */
+                const uint32_t sV = ring_base + (uint32_t)(warp * S + (int)((i + c) % S)) * kStage + kVOff;
+                if (KV8) {
+                    /* ldmatrix.trans on byte pairs: a lane gets V[2tig][d0], V[2tig][d0+1],
+                     * V[2tig+1][d0], V[2tig+1][d0+1] (d0 = 16u + 2gid); one byte permute
+                     * makes token pairs, converted to the A fragment whose rows gid / gid+8
+                     * are d0 / d0+1 (store_out_tile_kv8 undoes that order). */
 #pragma unroll
-            for (int mt = 0; mt < 8; ++mt) {
-                const int half = mt >> 2;
-                const int ch = ((2 * mt) + (mj & 1)) & 7;
-                const uint32_t addr = sV + half * kHalfBytes + tV * 128 + ((ch ^ mr) << 4);
-                uint32_t a0, a1, a2, a3;
-                ptx::ldsm_x4_t(addr, a0, a1, a2, a3);
-                ptx::mma_bf16_16816(o[mt], a0, a1, a2, a3, pb0, pb1);
+                    for (int c2 = 0; c2 < 4; ++c2) {
+                        const int u = 2 * c2 + (mj >> 1);
+                        const uint32_t addr = sV + tK * 128 + ((u ^ mr) << 4);
+                        uint32_t r[4];
+                        ptx::ldsm_x4_t(addr, r[0], r[1], r[2], r[3]);
+                        uint32_t x[4], y[4];
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) ptx::e4m3x4_to_f16(ptx::prmt(r[k], r[k], 0x3120u), x[k], y[k]);
+                        ptx::mma_f16_16816(o[2 * c2], x[0], y[0], x[1], y[1], pb0, pb1);
+                        ptx::mma_f16_16816(o[2 * c2 + 1], x[2], y[2], x[3], y[3], pb0, pb1);
+                    }
+                } else {
+#pragma unroll
+                    for (int mt = 0; mt < 8; ++mt) {
+                        const int half = mt >> 2;
+                        const int ch = ((2 * mt) + (mj & 1)) & 7;
+                        const uint32_t addr = sV + half * kHalfBytes + tV * 128 + ((ch ^ mr) << 4);
+                        uint32_t a0, a1, a2, a3;
+                        ptx::ldsm_x4_t(addr, a0, a1, a2, a3);
+                        ptx::mma_bf16_16816(o[mt], a0, a1, a2, a3, pb0, pb1);
+                    }
+                }
             }
             __syncwarp();
-            if (issued < ntot) issue_next();  // refills the stage just consumed
+#pragma unroll
+            for (int c = 0; c < NC; ++c)
+                if (issued < ntot) issue_next();  // refills the stages just consumed
 
-            const bool last_of_warp = (i == ntot - 1);
+            cc.c += NC - 1;  // the cursor now names the step's last chunk
+            const bool last_of_warp = (i + NC - 1 == ntot - 1);
             if (last_of_unit || last_of_warp) {
                 /* ---- finish this warp's part of the unit ---- */
                 float lA = l2[0], lB = l2[1];
@@ -518,9 +692,10 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
                     lA += __shfl_xor_sync(0xffffffffu, lA, off);
                     lB += __shfl_xor_sync(0xffffffffu, lB, off);
                 }
-                // a row with no visible key gives 0 (only with several query tokens)
-                const float invA = (!MQ || lA > 0.f) ? 1.f / lA : 0.f;
-                const float invB = (!MQ || lB > 0.f) ? 1.f / lB : 0.f;
+                // a row with no visible key gives 0 (only with several query tokens);
+                // FP8 pools fold V's dequantisation factor in here
+                const float invA = (!MQ || lA > 0.f) ? (KV8 ? vsc : 1.f) / lA : 0.f;
+                const float invB = (!MQ || lB > 0.f) ? (KV8 ? vsc : 1.f) / lB : 0.f;
                 const bool full = unit_start_seen && last_of_unit;
                 if (full) {
                     const int32_t kvh = cc.j / p.n_hg;
@@ -529,8 +704,8 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
                         p.out + row_offset<MQ>(p, cc.b, kvh, hg * kHeadsPerGroup + min(gid, nh_valid - 1));
 #pragma unroll
                     for (int mt = 0; mt < 8; ++mt)
-                        store_out_tile(orow, o[mt][0], o[mt][1], o[mt][2], o[mt][3], invA, invB, mt,
-                                       tig, gid < nh_valid);
+                        store_tile<KV8>(orow, o[mt][0], o[mt][1], o[mt][2], o[mt][3], invA, invB, mt,
+                                        tig, gid < nh_valid);
                 } else {
                     const float lseA = m2[0] + ptx::lg2(lA);
                     const float lseB = m2[1] + ptx::lg2(lB);
@@ -564,6 +739,17 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
             } else {
                 ++cc.c;
             }
+            return true;
+        };
+
+        while (i < ntot) {
+            if (kPair && i + 1 < ntot && cc.c + 1 < cc.n) {
+                if (!step(std::integral_constant<int, 2>{})) break;
+                i += 2;
+            } else {
+                if (!step(std::integral_constant<int, 1>{})) break;
+                i += 1;
+            }
         }
     }
 
@@ -575,7 +761,7 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
      * Parked state f = 2 * warp + slot lives at the start of warp `warp`'s ring; its key
      * (b, j), or (-1, -1) when empty, goes to a compact table for the run scan. */
     auto stash_addr = [&](int f) -> uint32_t {
-        return ring_base + (uint32_t)((f >> 1) * S * kStageBytes) + (uint32_t)((f & 1) * sizeof(Stash));
+        return ring_base + (uint32_t)((f >> 1) * S * kStage) + (uint32_t)((f & 1) * sizeof(Stash));
     };
     const uint32_t keys_base = ptx::smem_u32(misc + 32);  // int2 keys[2W], W <= 16
     {
@@ -659,7 +845,7 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
             const float invA = (!MQ || dA > 0.f) ? 1.f / dA : 0.f;
             const float invB = (!MQ || dB > 0.f) ? 1.f / dB : 0.f;
             if (inside) {
-                store_out_tile(orow, a0, a1, a2, a3, invA, invB, mt, tig, gid < nhv);
+                store_tile<KV8>(orow, a0, a1, a2, a3, invA, invB, mt, tig, gid < nhv);
                 continue;
             }
             const int64_t slot = record_slot(blockIdx.x, cs, ubeg);
@@ -713,7 +899,7 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
                 for (int u = 0; u < 16; ++u)
                     if (r0 + u < nrec) g.add(lse[u].x, lse[u].y, rv[u]);
             }
-            store_out_tile(orow, g.a0, g.a1, g.a2, g.a3, (!MQ || g.dA > 0.f) ? 1.f / g.dA : 0.f,
+            store_tile<KV8>(orow, g.a0, g.a1, g.a2, g.a3, (!MQ || g.dA > 0.f) ? 1.f / g.dA : 0.f,
                            (!MQ || g.dB > 0.f) ? 1.f / g.dB : 0.f, mt, tig, gid < nhv);
         }
     }
@@ -756,25 +942,26 @@ const Knobs& knobs() {
 
 constexpr int kDefaultWarps = 8;
 constexpr int kDefaultStages = 2;
+constexpr int kDefaultStagesKv8 = 4;  // 4 KB stages: the same bytes in flight as 2 x 8 KB
 constexpr int kDefaultMinChunks = 2;
 constexpr int kB200Sms = 148;
 constexpr int kB200SmemOptin = 232448;
 
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
-int smem_bytes_for(int warps, int stages, int64_t B) {
+int smem_bytes_for(int warps, int stages, int64_t B, bool kv8) {
     size_t s = 1024;  // alignment slack for the 1024-byte aligned ring
-    s += (size_t)warps * stages * kStageBytes;
+    s += (size_t)warps * stages * (kv8 ? kStageBytesKv8 : kStageBytes);
     s += (size_t)warps * stages * 8;
     s += 64 * 4;
     s += align_up((size_t)(B + 1) * 4, 16);
-    // The stash area reuses the ring; it must fit.
-    const size_t stash = (size_t)warps * 2 * sizeof(Stash);
-    if (stash > (size_t)warps * stages * kStageBytes) s += stash;
     return (int)s;
 }
 
-bool variant_compiled(int w, int s) {
+/* Instantiated (warps, stages) pairs.  A warp's two parked states reuse its own ring,
+ * so every pair must give a ring of at least 2 * sizeof(Stash) per warp. */
+bool variant_compiled(int w, int s, bool kv8) {
+    if (kv8) return w == 8 && (s == 3 || s == 4 || s == 6);
     return (w == 4 && (s >= 3 && s <= 6)) || (w == 8 && (s == 2 || s == 3));
 }
 
@@ -804,7 +991,7 @@ int64_t workspace_bytes_for(int64_t B, int64_t U, int grid) {
 }
 
 int make_plan_impl(int64_t B, int64_t Sq, int64_t Hq, int64_t Hkv, int64_t D, int64_t P, int sms,
-                   int smem_optin, pgqa_plan* plan) {
+                   int smem_optin, pgqa_plan* plan, bool kv8 = false) {
     memset(plan, 0, sizeof(*plan));
     int st = validate_shape(B, Hq, Hkv, D, P);
     if (st == PGQA_OK && (Sq <= 0 || Sq > 4096)) st = Sq <= 0 ? PGQA_ERR_BAD_SHAPE : PGQA_ERR_UNSUPPORTED;
@@ -817,14 +1004,15 @@ int make_plan_impl(int64_t B, int64_t Sq, int64_t Hq, int64_t Hkv, int64_t D, in
     const int64_t n_hg = ceil_div64(g * Sq, kHeadsPerGroup);
     const Knobs& kn = knobs();
     int w = kn.warps > 0 ? kn.warps : kDefaultWarps;
-    int s = kn.stages > 0 ? kn.stages : (w == 4 ? 6 : kDefaultStages);
-    if (!variant_compiled(w, s)) {
-        plan->status = PGQA_ERR_UNSUPPORTED;
-        return plan->status;
+    int s = kn.stages > 0 ? kn.stages : (kv8 ? kDefaultStagesKv8 : (w == 4 ? 6 : kDefaultStages));
+    if (!variant_compiled(w, s, kv8)) {
+        // a sweep knob that names no instantiation of this page format: use the defaults
+        w = kDefaultWarps;
+        s = kv8 ? kDefaultStagesKv8 : kDefaultStages;
     }
     // Deepest ring that fits next to the per-sequence prefix table.
-    while (smem_bytes_for(w, s, B) > smem_optin && variant_compiled(w, s - 1)) --s;
-    if (smem_bytes_for(w, s, B) > smem_optin) {
+    while (smem_bytes_for(w, s, B, kv8) > smem_optin && variant_compiled(w, s - 1, kv8)) --s;
+    if (smem_bytes_for(w, s, B, kv8) > smem_optin) {
         plan->status = PGQA_ERR_UNSUPPORTED;  // batch too large for the in-CTA prefix table
         return plan->status;
     }
@@ -834,7 +1022,7 @@ int make_plan_impl(int64_t B, int64_t Sq, int64_t Hq, int64_t Hkv, int64_t D, in
     plan->min_chunks_per_warp = kn.min_chunks > 0 ? kn.min_chunks : kDefaultMinChunks;
     plan->head_groups = (int32_t)n_hg;
     plan->units_per_seq = (int32_t)(Hkv * n_hg);
-    plan->smem_bytes = smem_bytes_for(w, s, B);
+    plan->smem_bytes = smem_bytes_for(w, s, B, kv8);
     plan->workspace_bytes = workspace_bytes_for(B, Hkv * n_hg, plan->grid_ctas);
     plan->status = PGQA_OK;
     return PGQA_OK;
@@ -897,16 +1085,23 @@ EncodeTiledFn encode_fn() {
 
 /* Tensor map over one pool viewed as (d: 128, kv: Hkv, token: num_pages*P), box
  * (64, 1, 16), 128-byte swizzle.  Out-of-range boxes read zeros (no fault). */
-int encode_pool_map(CUtensorMap* map, const void* base, int64_t Hkv, int64_t tokens) {
+int encode_pool_map(CUtensorMap* map, const void* base, int64_t Hkv, int64_t tokens,
+                    bool kv8 = false) {
     EncodeTiledFn fn = encode_fn();
     if (fn == nullptr) return PGQA_ERR_CUDA;
+    // FP8 pools: (d: 128 bytes, kv, token), box (128, 1, 16) -- one 2 KB box per chunk
+    const cuuint64_t row = kv8 ? kHeadDim : kHeadDim * 2;
     cuuint64_t dims[3] = {(cuuint64_t)kHeadDim, (cuuint64_t)Hkv, (cuuint64_t)tokens};
-    cuuint64_t strides[2] = {(cuuint64_t)kHeadDim * 2, (cuuint64_t)(Hkv * kHeadDim * 2)};
-    cuuint32_t box[3] = {64, 1, (cuuint32_t)kChunkTokens};
+    cuuint64_t strides[2] = {row, (cuuint64_t)Hkv * row};
+    cuuint32_t box[3] = {kv8 ? 128u : 64u, 1, (cuuint32_t)kChunkTokens};
     cuuint32_t estr[3] = {1, 1, 1};
-    CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims,
+    CUresult r = fn(map, kv8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3,
+                    const_cast<void*>(base), dims,
                     strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                    // promote to the token row's own size: a 256-byte promotion of a 128-byte
+                    // e4m3 row also fetches the neighbouring KV head's row, read much later
+                    kv8 ? CU_TENSOR_MAP_L2_PROMOTION_L2_128B : CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? PGQA_OK : PGQA_ERR_CUDA;
 }
 
@@ -944,10 +1139,12 @@ int lib_workspace(int dev, size_t need, void** out) {
     return PGQA_OK;
 }
 
-template <int W, int S, bool MQ = false>
+template <int W, int S, bool MQ, bool KV8>
 int launch_variant(const CUtensorMap& km, const CUtensorMap& vm, const DecodeParams& p, int grid,
                    int smem, cudaStream_t stream) {
-    auto kern = pgqa_decode_kernel<W, S, MQ>;
+    static_assert(2 * sizeof(Stash) <= (size_t)S * (KV8 ? kStageBytesKv8 : kStageBytes),
+                  "a warp's parked states must fit in its ring");
+    auto kern = pgqa_decode_kernel<W, S, MQ, KV8>;
     static int configured_smem[kMaxDevices] = {0};  // one table per instantiation
     int dev = 0;
     cudaGetDevice(&dev);
@@ -977,26 +1174,35 @@ int launch_variant(const CUtensorMap& km, const CUtensorMap& vm, const DecodePar
     return PGQA_OK;
 }
 
-template <bool MQ>
-int launch_mq(const pgqa_plan& plan, const CUtensorMap& km, const CUtensorMap& vm,
-              const DecodeParams& p, cudaStream_t stream) {
+template <bool MQ, bool KV8>
+int launch_t(const pgqa_plan& plan, const CUtensorMap& km, const CUtensorMap& vm,
+             const DecodeParams& p, cudaStream_t stream) {
     const int w = plan.warps_per_cta, s = plan.stages;
     const int g = plan.grid_ctas, sm = plan.smem_bytes;
-    if (w == 4 && s == 6) return launch_variant<4, 6, MQ>(km, vm, p, g, sm, stream);
-    if (w == 4 && s == 5) return launch_variant<4, 5, MQ>(km, vm, p, g, sm, stream);
-    if (w == 4 && s == 4) return launch_variant<4, 4, MQ>(km, vm, p, g, sm, stream);
-    if (w == 4 && s == 3) return launch_variant<4, 3, MQ>(km, vm, p, g, sm, stream);
-    if (w == 8 && s == 3) return launch_variant<8, 3, MQ>(km, vm, p, g, sm, stream);
-    if (w == 8 && s == 2) return launch_variant<8, 2, MQ>(km, vm, p, g, sm, stream);
+    if (KV8) {
+        if (w == 8 && s == 4) return launch_variant<8, 4, MQ, true>(km, vm, p, g, sm, stream);
+        if (w == 8 && s == 3) return launch_variant<8, 3, MQ, true>(km, vm, p, g, sm, stream);
+        if (w == 8 && s == 6) return launch_variant<8, 6, MQ, true>(km, vm, p, g, sm, stream);
+        return PGQA_ERR_UNSUPPORTED;
+    }
+    if (w == 4 && s == 6) return launch_variant<4, 6, MQ, false>(km, vm, p, g, sm, stream);
+    if (w == 4 && s == 5) return launch_variant<4, 5, MQ, false>(km, vm, p, g, sm, stream);
+    if (w == 4 && s == 4) return launch_variant<4, 4, MQ, false>(km, vm, p, g, sm, stream);
+    if (w == 4 && s == 3) return launch_variant<4, 3, MQ, false>(km, vm, p, g, sm, stream);
+    if (w == 8 && s == 3) return launch_variant<8, 3, MQ, false>(km, vm, p, g, sm, stream);
+    if (w == 8 && s == 2) return launch_variant<8, 2, MQ, false>(km, vm, p, g, sm, stream);
     return PGQA_ERR_UNSUPPORTED;
 }
 
 /* One query token (causal or not: an end-aligned mask hides nothing) takes the
  * single-token instantiation. */
 int launch(const pgqa_plan& plan, const CUtensorMap& km, const CUtensorMap& vm,
-           const DecodeParams& p, cudaStream_t stream) {
-    return p.Sq > 1 ? launch_mq<true>(plan, km, vm, p, stream)
-                    : launch_mq<false>(plan, km, vm, p, stream);
+           const DecodeParams& p, bool kv8, cudaStream_t stream) {
+    if (kv8)
+        return p.Sq > 1 ? launch_t<true, true>(plan, km, vm, p, stream)
+                        : launch_t<false, true>(plan, km, vm, p, stream);
+    return p.Sq > 1 ? launch_t<true, false>(plan, km, vm, p, stream)
+                    : launch_t<false, false>(plan, km, vm, p, stream);
 }
 
 int decode_impl(const void* q, const void* k, const void* v, void* out, const int32_t* seq_lens,
@@ -1004,11 +1210,13 @@ int decode_impl(const void* q, const void* k, const void* v, void* out, const in
                 int64_t P, int64_t num_pages, int64_t bt_stride, int64_t max_seqlen,
                 int64_t causal, float scale, void* workspace, size_t ws_bytes,
                 cudaStream_t stream, const void* k_new = nullptr, const void* v_new = nullptr,
-                int64_t len_add = 0) {
+                int64_t len_add = 0, bool kv8 = false, const float* k_scale = nullptr,
+                const float* v_scale = nullptr) {
     if (!q || !k || !v || !out || !seq_lens || !bt) return PGQA_ERR_NULL_POINTER;
     if (len_add < 0 || len_add > 4096) return len_add < 0 ? PGQA_ERR_BAD_SHAPE : PGQA_ERR_UNSUPPORTED;
     if (len_add > 0 && (!k_new || !v_new)) return PGQA_ERR_NULL_POINTER;
-    if ((reinterpret_cast<uintptr_t>(k_new) & 15) || (reinterpret_cast<uintptr_t>(v_new) & 15))
+    if ((reinterpret_cast<uintptr_t>(k_new) & 15) || (reinterpret_cast<uintptr_t>(v_new) & 15) ||
+        (reinterpret_cast<uintptr_t>(k_scale) & 3) || (reinterpret_cast<uintptr_t>(v_scale) & 3))
         return PGQA_ERR_MISALIGNED;
     int st = validate_shape(B, Hq, Hkv, D, P);
     if (st != PGQA_OK) return st;
@@ -1032,7 +1240,7 @@ int decode_impl(const void* q, const void* k, const void* v, void* out, const in
     st = device_info(dev, &di);
     if (st != PGQA_OK) return st;
     pgqa_plan plan;
-    st = make_plan_impl(B, Sq, Hq, Hkv, D, P, di.sms, di.smem_optin, &plan);
+    st = make_plan_impl(B, Sq, Hq, Hkv, D, P, di.sms, di.smem_optin, &plan, kv8);
     if (st != PGQA_OK) return st;
 
     if (workspace == nullptr) {
@@ -1044,9 +1252,9 @@ int decode_impl(const void* q, const void* k, const void* v, void* out, const in
     if (reinterpret_cast<uintptr_t>(workspace) & 255) return PGQA_ERR_MISALIGNED;
 
     CUtensorMap km, vm;
-    st = encode_pool_map(&km, k, Hkv, num_pages * P);
+    st = encode_pool_map(&km, k, Hkv, num_pages * P, kv8);
     if (st != PGQA_OK) return st;
-    st = encode_pool_map(&vm, v, Hkv, num_pages * P);
+    st = encode_pool_map(&vm, v, Hkv, num_pages * P, kv8);
     if (st != PGQA_OK) return st;
 
     const int64_t g = Hq / Hkv;
@@ -1073,6 +1281,8 @@ int decode_impl(const void* q, const void* k, const void* v, void* out, const in
     p.rows = (int32_t)(g * Sq);
     p.causal = (int32_t)causal;
     p.len_add = (int32_t)len_add;
+    p.k_scale = k_scale;
+    p.v_scale = v_scale;
     p.page_size = (int32_t)P;
     p.bt_stride = (int32_t)bt_stride;
     p.num_pages = (int32_t)num_pages;
@@ -1106,9 +1316,10 @@ int decode_impl(const void* q, const void* k, const void* v, void* out, const in
         a.bt_stride = (int32_t)bt_stride;
         a.num_pages = (int32_t)num_pages;
         a.cap_tokens = cap;
+        a.row_pieces_log2 = kv8 ? 3 : 4;
         if (launch_append(a, di.sms, stream) != 0) return PGQA_ERR_CUDA;
     }
-    return launch(plan, km, vm, p, stream);
+    return launch(plan, km, vm, p, kv8, stream);
 }
 
 }  // namespace
@@ -1189,35 +1400,34 @@ extern "C" int pgqa_decode_kvcache(const void* q, void* k_cache, void* v_cache,
                                   v_new, seqlen_new));
 }
 
-extern "C" int pgqa_append_kv(const void* k_new, const void* v_new, void* k_cache,
-                              void* v_cache, const int32_t* seq_lens,
-                              const int32_t* block_table, int64_t batch_size, int64_t seqlen_new,
-                              int64_t num_heads_k, int64_t headdim, int64_t page_size,
-                              int64_t num_pages, int64_t bt_stride, void* workspace,
-                              void* stream) {
+namespace {
+int append_entry(const void* k_new, const void* v_new, void* k_cache, void* v_cache,
+                 const int32_t* seq_lens, const int32_t* block_table, int64_t batch_size,
+                 int64_t seqlen_new, int64_t num_heads_k, int64_t headdim, int64_t page_size,
+                 int64_t num_pages, int64_t bt_stride, void* workspace, void* stream, bool kv8) {
     if (!k_new || !v_new || !k_cache || !v_cache || !seq_lens || !block_table)
-        return set_status(PGQA_ERR_NULL_POINTER);
+        return PGQA_ERR_NULL_POINTER;
     if (batch_size <= 0 || seqlen_new < 0 || num_heads_k <= 0 || page_size <= 0 ||
         num_pages <= 0 || bt_stride <= 0 || batch_size > INT32_MAX || seqlen_new > INT32_MAX ||
         num_heads_k > INT32_MAX || page_size > INT32_MAX || num_pages > INT32_MAX ||
         bt_stride > INT32_MAX)
-        return set_status(PGQA_ERR_BAD_SHAPE);
-    if (headdim != kHeadDim) return set_status(PGQA_ERR_UNSUPPORTED);
+        return PGQA_ERR_BAD_SHAPE;
+    if (headdim != kHeadDim) return PGQA_ERR_UNSUPPORTED;
     if ((reinterpret_cast<uintptr_t>(k_new) & 15) || (reinterpret_cast<uintptr_t>(v_new) & 15) ||
         (reinterpret_cast<uintptr_t>(k_cache) & 15) || (reinterpret_cast<uintptr_t>(v_cache) & 15) ||
         (reinterpret_cast<uintptr_t>(seq_lens) & 3) || (reinterpret_cast<uintptr_t>(block_table) & 3))
-        return set_status(PGQA_ERR_MISALIGNED);
+        return PGQA_ERR_MISALIGNED;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) {
         cudaGetLastError();
-        return set_status(PGQA_ERR_NO_DEVICE);
+        return PGQA_ERR_NO_DEVICE;
     }
     DevInfo di;
     int st = device_info(dev, &di);
-    if (st != PGQA_OK) return set_status(st);
+    if (st != PGQA_OK) return st;
     if (workspace == nullptr) {
         st = lib_workspace(dev, 256, &workspace);
-        if (st != PGQA_OK) return set_status(st);
+        if (st != PGQA_OK) return st;
     }
     AppendArgs a;
     a.k_new = static_cast<const uint4*>(k_new);
@@ -1234,9 +1444,47 @@ extern "C" int pgqa_append_kv(const void* k_new, const void* v_new, void* k_cach
     a.bt_stride = (int32_t)bt_stride;
     a.num_pages = (int32_t)num_pages;
     a.cap_tokens = bt_stride * page_size;
-    if (launch_append(a, di.sms, static_cast<cudaStream_t>(stream)) != 0)
-        return set_status(PGQA_ERR_CUDA);
-    return set_status(PGQA_OK);
+    a.row_pieces_log2 = kv8 ? 3 : 4;
+    if (launch_append(a, di.sms, static_cast<cudaStream_t>(stream)) != 0) return PGQA_ERR_CUDA;
+    return PGQA_OK;
+}
+}  // namespace
+
+extern "C" int pgqa_append_kv(const void* k_new, const void* v_new, void* k_cache,
+                              void* v_cache, const int32_t* seq_lens,
+                              const int32_t* block_table, int64_t batch_size, int64_t seqlen_new,
+                              int64_t num_heads_k, int64_t headdim, int64_t page_size,
+                              int64_t num_pages, int64_t bt_stride, void* workspace,
+                              void* stream) {
+    return set_status(append_entry(k_new, v_new, k_cache, v_cache, seq_lens, block_table,
+                                   batch_size, seqlen_new, num_heads_k, headdim, page_size,
+                                   num_pages, bt_stride, workspace, stream, false));
+}
+
+extern "C" int pgqa_append_kv_fp8(const void* k_new, const void* v_new, void* k_cache,
+                                  void* v_cache, const int32_t* seq_lens,
+                                  const int32_t* block_table, int64_t batch_size,
+                                  int64_t seqlen_new, int64_t num_heads_k, int64_t headdim,
+                                  int64_t page_size, int64_t num_pages, int64_t bt_stride,
+                                  void* workspace, void* stream) {
+    return set_status(append_entry(k_new, v_new, k_cache, v_cache, seq_lens, block_table,
+                                   batch_size, seqlen_new, num_heads_k, headdim, page_size,
+                                   num_pages, bt_stride, workspace, stream, true));
+}
+
+extern "C" int pgqa_decode_fp8(const void* q, void* k_cache, void* v_cache, const void* k_new,
+                               const void* v_new, void* out, const int32_t* seq_lens,
+                               const int32_t* block_table, int64_t batch_size, int64_t seqlen_q,
+                               int64_t seqlen_new, int64_t num_heads, int64_t num_heads_k,
+                               int64_t headdim, int64_t page_size, int64_t num_pages,
+                               int64_t bt_stride, int64_t max_seqlen, int64_t causal, float scale,
+                               const float* k_scale, const float* v_scale, void* workspace,
+                               size_t workspace_bytes, void* stream) {
+    return set_status(decode_impl(q, k_cache, v_cache, out, seq_lens, block_table, batch_size,
+                                  seqlen_q, num_heads, num_heads_k, headdim, page_size, num_pages,
+                                  bt_stride, max_seqlen, causal, scale, workspace,
+                                  workspace_bytes, static_cast<cudaStream_t>(stream), k_new,
+                                  v_new, seqlen_new, true, k_scale, v_scale));
 }
 
 static size_t workspace_size_impl(int64_t batch_size, int64_t seqlen_q, int64_t num_heads,

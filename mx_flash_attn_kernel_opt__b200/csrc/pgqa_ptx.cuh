@@ -13,6 +13,7 @@
 
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <stdint.h>
 
 namespace pgqa {
@@ -175,6 +176,34 @@ __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint3
 }
 
 /* Transpose one 8x8 b16 matrix held in the standard fragment layout. */
+__device__ __forceinline__ void mma_f16_16816(float (&d)[4], uint32_t a0, uint32_t a1,
+                                              uint32_t a2, uint32_t a3, uint32_t b0,
+                                              uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, "
+        "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+/* Four e4m3 bytes -> two f16x2 (exact: every e4m3 value is an f16 value).
+ * lo = (f16(byte0), f16(byte1)), hi = (f16(byte2), f16(byte3)), first element in the
+ * low half. */
+__device__ __forceinline__ void e4m3x4_to_f16(uint32_t r, uint32_t& lo, uint32_t& hi) {
+    asm("{\n\t.reg .b16 l16, h16;\n\t"
+        "mov.b32 {l16, h16}, %2;\n\t"
+        "cvt.rn.f16x2.e4m3x2 %0, l16;\n\t"
+        "cvt.rn.f16x2.e4m3x2 %1, h16;\n\t}"
+        : "=r"(lo), "=r"(hi)
+        : "r"(r));
+}
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+    return d;
+}
+
 __device__ __forceinline__ uint32_t movmatrix_t(uint32_t a) {
     uint32_t d;
     asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(a));
@@ -196,6 +225,11 @@ __device__ __forceinline__ float lg2(float x) {
 /* Pack two floats to bf16x2 (round-to-nearest-even); `lo` in the low half. */
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
     __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+    __half2 v = __floats2half2_rn(lo, hi);
     return *reinterpret_cast<uint32_t*>(&v);
 }
 

@@ -34,6 +34,8 @@ class DecodeInputs:
     scale: float
     name: str = ""
     seqlen_k: int = 0          # capacity the reference ABI passes as seqlen_k
+    k_scale: Optional[torch.Tensor] = None  # FP8 pools: [Hkv] float32 dequantisation factors
+    v_scale: Optional[torch.Tensor] = None
 
     @property
     def batch(self):
@@ -56,8 +58,9 @@ class DecodeInputs:
         return self.k.shape[0]
 
     def kv_bytes(self):
-        """Algorithmic K+V bytes of one call: sum_b L_b * Hkv * D * 2 B * 2."""
-        return int(self.seq_lens.to(torch.int64).sum().item()) * self.num_heads_k * HEAD_DIM * 4
+        """Algorithmic K+V bytes of one call: sum_b L_b * Hkv * D * (element bytes) * 2."""
+        return (int(self.seq_lens.to(torch.int64).sum().item()) * self.num_heads_k * HEAD_DIM
+                * 2 * self.k.element_size())
 
     def algorithmic_bytes(self):
         """KV bytes + q and out + the block-table entries and lengths actually read."""
@@ -67,9 +70,11 @@ class DecodeInputs:
         return self.kv_bytes() + 2 * B * Hq * HEAD_DIM * 2 + pages * 4 + B * 4
 
     def to(self, device):
+        mv = (lambda t: None if t is None else t.to(device))
         return dataclasses.replace(
             self, q=self.q.to(device), k=self.k.to(device), v=self.v.to(device),
-            block_table=self.block_table.to(device), seq_lens=self.seq_lens.to(device))
+            block_table=self.block_table.to(device), seq_lens=self.seq_lens.to(device),
+            k_scale=mv(self.k_scale), v_scale=mv(self.v_scale))
 
     def digest(self):
         """sha256 over every input byte (detects generator drift between machines)."""
@@ -288,12 +293,55 @@ def custom_case(B, Hq, Hkv, P, seq_lens, seed=0, table="permuted", spare_pages=0
     return inp.to(device) if device != "cpu" else inp
 
 
+FP8_MAX = 448.0  # largest finite float8_e4m3fn
+
+
+def to_fp8(inp: DecodeInputs, k_scale=None, v_scale=None, keep_device=False):
+    """The same case with float8_e4m3fn pools: per KV head, element / scale rounded to
+    e4m3 (scale = that head's max |x| / 448 unless given).  Returns a new DecodeInputs
+    carrying k_scale / v_scale ([Hkv] float32), on the CPU unless `keep_device` (then on
+    the pools' device, converted a block of pages at a time)."""
+    if not keep_device:
+        inp = inp.to("cpu")
+    Hkv = inp.num_heads_k
+    step = max(1, (1 << 28) // max(1, inp.k[0].numel() * 4))  # ~256 MB of fp32 per block
+
+    def quant(pool, scale):
+        if scale is None:
+            amax = torch.zeros(Hkv, dtype=torch.float32, device=pool.device)
+            for i in range(0, pool.shape[0], step):
+                amax = torch.maximum(amax, pool[i:i + step].float().abs().amax(dim=(0, 1, 3)))
+            scale = amax.clamp(min=1e-6) / FP8_MAX
+        scale = torch.as_tensor(scale, dtype=torch.float32).reshape(-1).expand(Hkv)
+        scale = scale.to(pool.device).contiguous()
+        y = torch.empty(pool.shape, dtype=torch.float8_e4m3fn, device=pool.device)
+        for i in range(0, pool.shape[0], step):
+            x = pool[i:i + step].float() / scale.view(1, 1, Hkv, 1)
+            y[i:i + step] = x.clamp(-FP8_MAX, FP8_MAX).to(torch.float8_e4m3fn)
+        return y, scale
+
+    k8, ks = quant(inp.k, k_scale)
+    v8, vs = quant(inp.v, v_scale)
+    return dataclasses.replace(inp, k=k8, v=v8, k_scale=ks, v_scale=vs,
+                               name=inp.name + "+fp8")
+
+
+def dequant(pool, scale):
+    """float32 values of an e4m3 pool with per-KV-head factors (test helper)."""
+    return pool.float() * scale.float().view(1, 1, -1, 1)
+
+
 def poison(inp: DecodeInputs, value=float("nan")):
     """Fill every KV slot that a correct kernel must not read with `value`:
     pages no valid block-table entry references (including the targets of padding
-    slots) and the slots past seq_len inside each sequence's last page.
-    Returns a new DecodeInputs (CPU tensors)."""
+    slots) and the slots past seq_len inside each sequence's last page.  FP8 pools get
+    the e4m3 NaN pattern (0x7f).  Returns a new DecodeInputs (CPU tensors)."""
     inp = inp.to("cpu")
+    if inp.k.dtype == torch.float8_e4m3fn:
+        pk = poison(dataclasses.replace(inp, k=inp.k.view(torch.uint8), v=inp.v.view(torch.uint8)),
+                    value=0x7F)
+        return dataclasses.replace(inp, k=pk.k.view(torch.float8_e4m3fn),
+                                   v=pk.v.view(torch.float8_e4m3fn), name=inp.name + "+poison")
     k, v = inp.k.clone(), inp.v.clone()
     P = inp.page_size
     used = torch.zeros(inp.num_pages, dtype=torch.bool)

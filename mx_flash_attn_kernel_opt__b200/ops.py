@@ -47,9 +47,13 @@ def workspace_for(batch_size, num_heads, num_heads_k, headdim, page_size, device
     return ws
 
 
+FP8 = torch.float8_e4m3fn
+
+
 def _check_tensors(q, k, v, out, seq_lens, block_table):
-    for name, t, dt in (("q", q, torch.bfloat16), ("k", k, torch.bfloat16),
-                        ("v", v, torch.bfloat16), ("out", out, torch.bfloat16),
+    kv_dt = k.dtype if k.dtype in (torch.bfloat16, FP8) else torch.bfloat16
+    for name, t, dt in (("q", q, torch.bfloat16), ("k", k, kv_dt),
+                        ("v", v, kv_dt), ("out", out, torch.bfloat16),
                         ("seq_lens", seq_lens, torch.int32),
                         ("block_table", block_table, torch.int32)):
         if not t.is_cuda:
@@ -60,18 +64,36 @@ def _check_tensors(q, k, v, out, seq_lens, block_table):
             raise ValueError(f"{name} must be contiguous")
 
 
+def _scale_array(x, Hkv, device):
+    """Per-KV-head dequantisation factors as a float32 device tensor (None stays None)."""
+    if x is None:
+        return None
+    if not torch.is_tensor(x):
+        x = torch.full((Hkv,), float(x), dtype=torch.float32)
+    x = x.to(device=device, dtype=torch.float32).reshape(-1)
+    if x.numel() == 1:
+        x = x.expand(Hkv)
+    if x.numel() != Hkv:
+        raise PgqaError(2, "k_scale / v_scale must hold one value or one per KV head")
+    return x.contiguous()
+
+
 def decode(q, k_cache, v_cache, block_table, seq_lens, scale=None, out=None,
-           max_seqlen=0, workspace=None, causal=False, k_new=None, v_new=None):
+           max_seqlen=0, workspace=None, causal=False, k_new=None, v_new=None,
+           k_scale=None, v_scale=None):
     """Paged GQA decode.
 
-    q [B, Hq, D] (one query token) or [B, Sq, Hq, D]; k_cache/v_cache
-    [num_pages, P, Hkv, D] (bf16); block_table [B, stride] int32; seq_lens [B] int32.
-    With Sq > 1 and `causal`, query token i sees keys [0, L - Sq + i].
+    q [B, Hq, D] (one query token) or [B, Sq, Hq, D] bf16; k_cache/v_cache
+    [num_pages, P, Hkv, D], bf16 or float8_e4m3fn; block_table [B, stride] int32;
+    seq_lens [B] int32.  With Sq > 1 and `causal`, query token i sees keys [0, L - Sq + i].
 
-    k_new / v_new [B, S_new, Hkv, D] (optional, as flash_attn_with_kvcache's k / v): the
-    new tokens are first written into the pools at positions [L_b, L_b + S_new) and the
-    decode then runs over L_b + S_new keys (seq_lens holds the lengths before the append
-    and is not modified).  Returns out (same shape as q).
+    k_new / v_new [B, S_new, Hkv, D] (optional, as flash_attn_with_kvcache's k / v, in
+    the pools' dtype): the new tokens are first written into the pools at positions
+    [L_b, L_b + S_new) and the decode then runs over L_b + S_new keys (seq_lens holds
+    the lengths before the append and is not modified).
+
+    FP8 pools: an element of KV head h is worth e4m3 * k_scale[h] (v_scale for V);
+    k_scale / v_scale are floats or [Hkv] tensors (None = 1).  Returns out (q's shape).
     """
     if out is None:
         out = torch.empty_like(q)
@@ -84,14 +106,29 @@ def decode(q, k_cache, v_cache, block_table, seq_lens, scale=None, out=None,
         raise PgqaError(2, "decode: K/V pool shapes")
     if block_table.dim() != 2 or block_table.shape[0] != B or seq_lens.shape != (B,):
         raise PgqaError(2, "decode: block_table / seq_lens shapes")
-    S_new = _check_new_tokens(k_new, v_new, B, Hkv, D)
+    fp8 = k_cache.dtype == FP8
+    S_new = _check_new_tokens(k_new, v_new, B, Hkv, D, k_cache.dtype)
+    if not fp8 and (k_scale is not None or v_scale is not None):
+        raise ValueError("k_scale / v_scale apply to float8_e4m3fn pools only")
     if scale is None:
         scale = 1.0 / math.sqrt(D)
     if workspace is None:
         workspace = workspace_for(B, Hq, Hkv, D, P, q.device, seqlen_q=Sq)
     L = lib()
     with torch.cuda.device(q.device):
-        if S_new == 0:
+        if fp8:
+            ks = _scale_array(k_scale, Hkv, q.device)
+            vs = _scale_array(v_scale, Hkv, q.device)
+            st = L.pgqa_decode_fp8(_ptr(q), _ptr(k_cache), _ptr(v_cache),
+                                   _ptr(k_new) if S_new else None,
+                                   _ptr(v_new) if S_new else None, _ptr(out), _ptr(seq_lens),
+                                   _ptr(block_table), B, Sq, S_new, Hq, Hkv, D, P, num_pages,
+                                   block_table.stride(0), max_seqlen, int(bool(causal)),
+                                   float(scale), _ptr(ks) if ks is not None else None,
+                                   _ptr(vs) if vs is not None else None, _ptr(workspace),
+                                   workspace.numel(), _stream_handle(q.device))
+            what = "pgqa_decode_fp8"
+        elif S_new == 0:
             st = L.pgqa_decode_v2(_ptr(q), _ptr(k_cache), _ptr(v_cache), _ptr(out),
                                   _ptr(seq_lens), _ptr(block_table), B, Sq, Hq, Hkv, D, P,
                                   num_pages, block_table.stride(0), max_seqlen,
@@ -110,15 +147,15 @@ def decode(q, k_cache, v_cache, block_table, seq_lens, scale=None, out=None,
     return out
 
 
-def _check_new_tokens(k_new, v_new, B, Hkv, D):
+def _check_new_tokens(k_new, v_new, B, Hkv, D, dtype):
     """Validates the appended tokens; returns S_new (0 when none are given)."""
     if k_new is None and v_new is None:
         return 0
     if k_new is None or v_new is None:
         raise ValueError("k_new and v_new go together")
     for name, t in (("k_new", k_new), ("v_new", v_new)):
-        if not t.is_cuda or t.dtype != torch.bfloat16 or not t.is_contiguous():
-            raise ValueError(f"{name} must be a contiguous bf16 CUDA tensor")
+        if not t.is_cuda or t.dtype != dtype or not t.is_contiguous():
+            raise ValueError(f"{name} must be a contiguous {dtype} CUDA tensor")
     if k_new.dim() != 4 or tuple(k_new.shape) != tuple(v_new.shape) or \
             k_new.shape[0] != B or k_new.shape[2] != Hkv or k_new.shape[3] != D:
         raise PgqaError(2, "k_new / v_new must be [B, S_new, Hkv, D]")
@@ -126,24 +163,25 @@ def _check_new_tokens(k_new, v_new, B, Hkv, D):
 
 
 def append_kv(k_new, v_new, k_cache, v_cache, block_table, seq_lens, workspace=None):
-    """Write k_new / v_new [B, S_new, Hkv, D] into the pools at positions
-    [L_b, L_b + S_new) of each sequence (seq_lens = lengths before the append; not
-    modified).  Asynchronous on torch's current stream."""
-    for name, t, dt in (("k_cache", k_cache, torch.bfloat16), ("v_cache", v_cache, torch.bfloat16),
+    """Write k_new / v_new [B, S_new, Hkv, D] into the pools (bf16 or float8_e4m3fn) at
+    positions [L_b, L_b + S_new) of each sequence (seq_lens = lengths before the append;
+    not modified).  Asynchronous on torch's current stream."""
+    kv_dt = k_cache.dtype if k_cache.dtype in (torch.bfloat16, FP8) else torch.bfloat16
+    for name, t, dt in (("k_cache", k_cache, kv_dt), ("v_cache", v_cache, kv_dt),
                         ("seq_lens", seq_lens, torch.int32),
                         ("block_table", block_table, torch.int32)):
         if not t.is_cuda or t.dtype != dt or not t.is_contiguous():
             raise ValueError(f"{name} must be a contiguous {dt} CUDA tensor")
     num_pages, P, Hkv, D = k_cache.shape
     B = block_table.shape[0]
-    S_new = _check_new_tokens(k_new, v_new, B, Hkv, D)
+    S_new = _check_new_tokens(k_new, v_new, B, Hkv, D, k_cache.dtype)
     L = lib()
+    fn = L.pgqa_append_kv_fp8 if k_cache.dtype == FP8 else L.pgqa_append_kv
     with torch.cuda.device(k_cache.device):
-        st = L.pgqa_append_kv(_ptr(k_new), _ptr(v_new), _ptr(k_cache), _ptr(v_cache),
-                              _ptr(seq_lens), _ptr(block_table), B, S_new, Hkv, D, P,
-                              num_pages, block_table.stride(0),
-                              _ptr(workspace) if workspace is not None else None,
-                              _stream_handle(k_cache.device))
+        st = fn(_ptr(k_new), _ptr(v_new), _ptr(k_cache), _ptr(v_cache), _ptr(seq_lens),
+                _ptr(block_table), B, S_new, Hkv, D, P, num_pages, block_table.stride(0),
+                _ptr(workspace) if workspace is not None else None,
+                _stream_handle(k_cache.device))
     check(st, "pgqa_append_kv")
 
 

@@ -12,6 +12,7 @@ tests/golden/gen_golden.py).
 from .append_kv import append_kv_ref  # noqa: F401
 from .paged_decode import (  # noqa: F401
     lse_combine_ref,
+    paged_decode_fp8_ref,
     paged_decode_ref,
     split_partials_ref,
     split_decode_ref,

@@ -71,6 +71,20 @@ def paged_decode_ref(q, k_cache, v_cache, block_table, seq_lens, scale=None, row
     return out[:, 0] if squeeze else out
 
 
+def paged_decode_fp8_ref(q, k8, v8, k_scale, v_scale, block_table, seq_lens, scale=None,
+                         causal=False):
+    """FP8 KV pages: the value of an element of KV head h is e4m3 * k_scale[h]
+    (v_scale[h] for V).  The e4m3 bytes are decoded by torch's float8_e4m3fn conversion
+    (OCP e4m3fn: bias 7, NaN = S.1111.111, no infinities), dequantised in fp32 and fed
+    to paged_decode_ref."""
+    Hkv = k8.shape[2]
+    ks = torch.as_tensor(k_scale, dtype=torch.float32).reshape(-1).expand(Hkv).cpu()
+    vs = torch.as_tensor(v_scale, dtype=torch.float32).reshape(-1).expand(Hkv).cpu()
+    kd = k8.cpu().float() * ks.view(1, 1, Hkv, 1)
+    vd = v8.cpu().float() * vs.view(1, 1, Hkv, 1)
+    return paged_decode_ref(q, kd, vd, block_table, seq_lens, scale=scale, causal=causal)
+
+
 LOG2E = 1.4426950408889634
 
 

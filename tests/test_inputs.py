@@ -67,3 +67,26 @@ def test_algorithmic_bytes():
     inp = inputs.custom_case(2, 8, 2, 16, [16, 17], seed=0)
     assert inp.kv_bytes() == 33 * 2 * 128 * 4
     assert inp.algorithmic_bytes() == inp.kv_bytes() + 2 * 2 * 8 * 128 * 2 + 3 * 4 + 2 * 4
+
+
+def test_fp8_pools_quantise_per_head_and_poison_with_nan():
+    from oracle import paged_decode_fp8_ref, paged_decode_ref
+    inp = inputs.custom_case(3, 8, 2, 16, [5, 40, 17], seed=1, spare_pages=2)
+    f = inputs.to_fp8(inp)
+    assert f.k.dtype == torch.float8_e4m3fn and f.k_scale.shape == (2,)
+    assert f.kv_bytes() * 2 == inp.kv_bytes()
+    # per-head scale maps the head's max |x| to 448 (the largest e4m3fn value)
+    for h in range(2):
+        assert abs(f.k[:, :, h].float().abs().max().item() - 448.0) < 1e-3
+    # dequantised values stay within e4m3's half-ulp (2^-4 relative) of the bf16 ones
+    d = inputs.dequant(f.k, f.k_scale)
+    x = inp.k.float()
+    assert ((d - x).abs() <= x.abs() * 2 ** -4 + f.k_scale.max() * 2 ** -9).all()
+    # poisoning writes the e4m3 NaN pattern only where a correct kernel never reads
+    pz = inputs.poison(f)
+    assert torch.isnan(pz.k.float()).any()
+    ref = paged_decode_fp8_ref(inp.q, pz.k, pz.v, f.k_scale, f.v_scale, pz.block_table,
+                               pz.seq_lens)
+    assert torch.isfinite(ref).all()
+    ref2 = paged_decode_ref(inp.q, d, inputs.dequant(f.v, f.v_scale), f.block_table, f.seq_lens)
+    assert torch.allclose(ref, ref2, atol=1e-6)
