@@ -253,13 +253,22 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
     constexpr int NT = W * 32;
     constexpr int kStage = KV8 ? kStageBytesKv8 : kStageBytes;
     constexpr int kVOff = KV8 ? kHalfBytes : 2 * kHalfBytes;  // V's offset inside a stage
+    // FP8: a warp's first cut unit goes straight to its own shared-memory slot when it
+    // completes (frees 32 registers for more warps); bf16 keeps it in registers.
+    constexpr bool kEarlyStash = KV8;
+    constexpr int kMiscInts = 32 + 4 * W;  // warp sums [32] + parked keys int2[2W]
+    static_assert((kEarlyStash ? 1 : 2) * sizeof(Stash) <= (size_t)S * kStage,
+                  "the states a warp parks in its ring must fit in it");
+    static_assert(2 * W <= 32, "parked states are scanned one per lane");
     extern __shared__ uint8_t smem_raw[];
     // 128-byte TMA swizzle needs 1024-byte aligned stages (shared-window offset).
     uint8_t* smem = smem_raw + ((1024u - (ptx::smem_u32(smem_raw) & 1023u)) & 1023u);
     uint8_t* ring = smem;                                                  // W*S stages
     uint64_t* bars = reinterpret_cast<uint64_t*>(ring + W * S * kStage);   // W*S
-    int32_t* misc = reinterpret_cast<int32_t*>(bars + W * S);               // 64 ints
-    uint32_t* pre = reinterpret_cast<uint32_t*>(misc + 64);                 // B+1
+    int32_t* misc = reinterpret_cast<int32_t*>(bars + W * S);               // kMiscInts
+    uint32_t* pre = reinterpret_cast<uint32_t*>(misc + kMiscInts);          // B+1
+    // early stash slots (kEarlyStash): W x Stash after the prefix table, 16-byte aligned
+    const uint32_t early_base = (ptx::smem_u32(pre + p.B + 1) + 15u) & ~15u;
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
@@ -710,12 +719,23 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
                     const float lseA = m2[0] + ptx::lg2(lA);
                     const float lseB = m2[1] + ptx::lg2(lB);
                     if (units_done == 0) {
+                        if (kEarlyStash) {
+                            const uint32_t a0 = early_base + (uint32_t)(warp * sizeof(Stash));
 #pragma unroll
-                        for (int mt = 0; mt < 8; ++mt) {
-                            fo[mt][0] = o[mt][0] * invA; fo[mt][1] = o[mt][1] * invB;
-                            fo[mt][2] = o[mt][2] * invA; fo[mt][3] = o[mt][3] * invB;
+                            for (int mt = 0; mt < 8; ++mt)
+                                ptx::sts_f4(a0 + (mt * 32 + lane) * 16,
+                                            make_float4(o[mt][0] * invA, o[mt][1] * invB,
+                                                        o[mt][2] * invA, o[mt][3] * invB));
+                            if (gid == 0)
+                                ptx::sts_f2(a0 + offsetof(Stash, lse) + tig * 8, make_float2(lseA, lseB));
+                        } else {
+#pragma unroll
+                            for (int mt = 0; mt < 8; ++mt) {
+                                fo[mt][0] = o[mt][0] * invA; fo[mt][1] = o[mt][1] * invB;
+                                fo[mt][2] = o[mt][2] * invA; fo[mt][3] = o[mt][3] * invB;
+                            }
+                            flse[0] = lseA; flse[1] = lseB;
                         }
-                        flse[0] = lseA; flse[1] = lseB;
                         first_u = cc;
                         have_first = true;
                     } else {
@@ -758,17 +778,22 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
     ptx::griddep_launch_dependents();
 
     /* ---- park this warp's cut units in its own (now idle) ring: no TMA is in flight ----
-     * Parked state f = 2 * warp + slot lives at the start of warp `warp`'s ring; its key
-     * (b, j), or (-1, -1) when empty, goes to a compact table for the run scan. */
+     * Parked state f = 2 * warp + slot lives at the start of warp `warp`'s ring (slot 0
+     * in the early-stash slot when kEarlyStash); its key (b, j), or (-1, -1) when empty,
+     * goes to a compact table for the run scan. */
     auto stash_addr = [&](int f) -> uint32_t {
+        if (kEarlyStash) {  // slot 0 in the early-stash slot, slot 1 at the ring's start
+            if (!(f & 1)) return early_base + (uint32_t)((f >> 1) * sizeof(Stash));
+            return ring_base + (uint32_t)((f >> 1) * S * kStage);
+        }
         return ring_base + (uint32_t)((f >> 1) * S * kStage) + (uint32_t)((f & 1) * sizeof(Stash));
     };
-    const uint32_t keys_base = ptx::smem_u32(misc + 32);  // int2 keys[2W], W <= 16
+    const uint32_t keys_base = ptx::smem_u32(misc + 32);  // int2 keys[2W]
     {
         const bool v0 = (warp < wa) && have_first && !aborted;
         const bool v1 = (warp < wa) && have_last && !aborted;
         const uint32_t a0 = stash_addr(2 * warp), a1 = stash_addr(2 * warp + 1);
-        if (v0) {
+        if (v0 && !kEarlyStash) {
 #pragma unroll
             for (int mt = 0; mt < 8; ++mt)
                 ptx::sts_f4(a0 + (mt * 32 + lane) * 16, make_float4(fo[mt][0], fo[mt][1], fo[mt][2], fo[mt][3]));
@@ -953,15 +978,16 @@ int smem_bytes_for(int warps, int stages, int64_t B, bool kv8) {
     size_t s = 1024;  // alignment slack for the 1024-byte aligned ring
     s += (size_t)warps * stages * (kv8 ? kStageBytesKv8 : kStageBytes);
     s += (size_t)warps * stages * 8;
-    s += 64 * 4;
-    s += align_up((size_t)(B + 1) * 4, 16);
+    s += (size_t)(32 + 4 * warps) * 4;           // warp sums + parked keys
+    s += align_up((size_t)(B + 1) * 4, 16) + 16;  // prefix table (+ alignment of what follows)
+    if (kv8) s += (size_t)warps * sizeof(Stash);  // early stash slots
     return (int)s;
 }
 
 /* Instantiated (warps, stages) pairs.  A warp's two parked states reuse its own ring,
  * so every pair must give a ring of at least 2 * sizeof(Stash) per warp. */
 bool variant_compiled(int w, int s, bool kv8) {
-    if (kv8) return w == 8 && (s == 3 || s == 4 || s == 6);
+    if (kv8) return (w == 8 && (s == 3 || s == 4 || s == 6)) || (w == 12 && s == 3);
     return (w == 4 && (s >= 3 && s <= 6)) || (w == 8 && (s == 2 || s == 3));
 }
 
@@ -1142,8 +1168,6 @@ int lib_workspace(int dev, size_t need, void** out) {
 template <int W, int S, bool MQ, bool KV8>
 int launch_variant(const CUtensorMap& km, const CUtensorMap& vm, const DecodeParams& p, int grid,
                    int smem, cudaStream_t stream) {
-    static_assert(2 * sizeof(Stash) <= (size_t)S * (KV8 ? kStageBytesKv8 : kStageBytes),
-                  "a warp's parked states must fit in its ring");
     auto kern = pgqa_decode_kernel<W, S, MQ, KV8>;
     static int configured_smem[kMaxDevices] = {0};  // one table per instantiation
     int dev = 0;
@@ -1180,6 +1204,7 @@ int launch_t(const pgqa_plan& plan, const CUtensorMap& km, const CUtensorMap& vm
     const int w = plan.warps_per_cta, s = plan.stages;
     const int g = plan.grid_ctas, sm = plan.smem_bytes;
     if (KV8) {
+        if (w == 12 && s == 3) return launch_variant<12, 3, MQ, true>(km, vm, p, g, sm, stream);
         if (w == 8 && s == 4) return launch_variant<8, 4, MQ, true>(km, vm, p, g, sm, stream);
         if (w == 8 && s == 3) return launch_variant<8, 3, MQ, true>(km, vm, p, g, sm, stream);
         if (w == 8 && s == 6) return launch_variant<8, 6, MQ, true>(km, vm, p, g, sm, stream);
