@@ -40,3 +40,45 @@ def gather_heads(out_local, group=None):
     buf = torch.empty((world * B, hq_local, D), dtype=out_local.dtype, device=out_local.device)
     dist.all_gather_into_tensor(buf, out_local.contiguous(), group=group)
     return buf.view(world, B, hq_local, D).permute(1, 0, 2, 3).reshape(B, world * hq_local, D)
+
+
+class PeerFailure(RuntimeError):
+    """A rank did not report for a step within the timeout."""
+
+    def __init__(self, step, missing):
+        self.step = step
+        self.missing = list(missing)
+        super().__init__(f"step {step}: no report from rank(s) {self.missing}")
+
+
+class StepCheck:
+    """Host-side liveness check between decode steps (no GPU involvement).
+
+    Every rank calls `arrive(step)` before its next launch or collective; it records the
+    rank's report in a key-value store (a torch.distributed TCPStore) and waits, at most
+    `timeout_s`, for every other rank's report of the same step.  A rank that died or
+    left between steps never reports, so the survivors raise PeerFailure naming it
+    before they launch anything that would wait on it -- instead of blocking in the next
+    collective until the process-group timeout.
+    """
+
+    def __init__(self, store, rank, world_size, timeout_s=10.0, prefix="pgqa"):
+        self.store = store
+        self.rank = rank
+        self.world = world_size
+        self.timeout_s = float(timeout_s)
+        self.prefix = prefix
+
+    def _key(self, step, rank):
+        return f"{self.prefix}/step{step}/rank{rank}"
+
+    def arrive(self, step):
+        import datetime
+
+        self.store.set(self._key(step, self.rank), "1")
+        keys = [self._key(step, r) for r in range(self.world)]
+        try:
+            self.store.wait(keys, datetime.timedelta(seconds=self.timeout_s))
+        except Exception:
+            missing = [r for r in range(self.world) if not self.store.check([self._key(step, r)])]
+            raise PeerFailure(step, missing) from None

@@ -12,6 +12,41 @@ REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 sys.path.insert(0, REPO)
 
 
+def failing_peer():
+    """Host-side failure detection, CPU only: a 3-step decode loop over gloo ranks in
+    which the last rank exits after step 0.  The survivors must name it through
+    sharding.StepCheck before their next collective (printed as PEER_FAILURE)."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from mx_flash_attn_kernel_opt__b200 import inputs, sharding
+    from oracle import paged_decode_ref
+
+    rank = int(os.environ["RANK"])
+    world = int(os.environ["WORLD_SIZE"])
+    store = dist.TCPStore("127.0.0.1", int(os.environ["MASTER_PORT"]) + 1, world,
+                          is_master=(rank == 0), timeout=datetime.timedelta(seconds=30))
+    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=20))
+    check = sharding.StepCheck(store, rank, world, timeout_s=3.0)
+    full = inputs.baseline_config("c1")
+    q, k, v = sharding.shard_tensors(full.q, full.k, full.v, rank, world)
+    for step in range(3):
+        if rank == world - 1 and step == 1:
+            print(f"rank{rank} leaving after step 0", flush=True)
+            os._exit(5)  # between steps: nothing of this rank is in flight
+        try:
+            check.arrive(step)
+        except sharding.PeerFailure as e:
+            print(f"rank{rank} PEER_FAILURE step={e.step} missing={e.missing}", flush=True)
+            os._exit(0)
+        out = paged_decode_ref(q, k, v, full.block_table, full.seq_lens).to(torch.bfloat16)
+        sharding.gather_heads(out)
+        print(f"rank{rank} step {step} done", flush=True)
+    os._exit(4)  # the failure was not detected
+
+
 def main():
     import datetime
 
@@ -22,6 +57,8 @@ def main():
     from oracle import match_stats, paged_decode_ref
 
     backend = sys.argv[1]
+    if backend == "gloo-fail":
+        failing_peer()
     rank = int(os.environ["RANK"])
     world = int(os.environ["WORLD_SIZE"])
     if backend == "nccl":

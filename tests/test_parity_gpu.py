@@ -244,3 +244,23 @@ def test_expired_wait_reports_timeout_and_context_survives(cuda_device, monkeypa
     pgqa.check_device_error(ws)
     ref = paged_decode_ref(inp.q, inp.k, inp.v, inp.block_table, inp.seq_lens)
     assert_parity(out, ref, what="after timeout")
+
+
+def test_undersized_or_misaligned_workspace_is_refused(cuda_device):
+    """A caller workspace below pgqa_workspace_size, or not 256-byte aligned, is refused
+    before anything is launched (the output is left untouched)."""
+    inp = inputs.baseline_config("c1").to(cuda_device)
+    out = torch.full_like(inp.q, 7.0)
+    small = torch.zeros(1024, dtype=torch.uint8, device=cuda_device)
+    with pytest.raises(pgqa.PgqaError) as e:
+        pgqa.decode(inp.q, inp.k, inp.v, inp.block_table, inp.seq_lens, out=out, workspace=small)
+    assert e.value.status == 5
+    need = _lib.lib().pgqa_workspace_size(inp.batch, inp.num_heads, inp.num_heads_k, 128,
+                                          inp.page_size)
+    big = torch.zeros(need + 512, dtype=torch.uint8, device=cuda_device)
+    with pytest.raises(pgqa.PgqaError) as e:
+        pgqa.decode(inp.q, inp.k, inp.v, inp.block_table, inp.seq_lens, out=out,
+                    workspace=big[16:])
+    assert e.value.status == 4
+    torch.cuda.synchronize(cuda_device)
+    assert bool((out == 7.0).all())

@@ -63,3 +63,31 @@ def test_nccl_two_gpus_gather_matches_unsharded_oracle():
         pytest.skip("needs 2 GPUs")
     r = _torchrun(2, "nccl", 300)
     assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-4000:]
+
+
+def test_step_check_names_a_rank_that_left():
+    """Failure detection on the host (gloo, CPU): rank 1 exits between steps; rank 0's
+    StepCheck raises PeerFailure naming it within the 3 s limit, instead of waiting in
+    the next all-gather.  Processes are started directly (not through torchrun, whose
+    agent would stop the survivor when one worker exits)."""
+    port = _free_port()
+    procs = []
+    for r in range(2):
+        env = dict(os.environ, RANK=str(r), WORLD_SIZE="2", LOCAL_RANK=str(r),
+                   MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), OMP_NUM_THREADS="2")
+        procs.append(subprocess.Popen([sys.executable, os.path.join(HERE, "shard_worker.py"),
+                                       "gloo-fail"], env=env, stdout=subprocess.PIPE,
+                                      stderr=subprocess.STDOUT, text=True))
+    outs = []
+    for pr in procs:
+        try:
+            out, _ = pr.communicate(timeout=180)
+        except subprocess.TimeoutExpired:
+            pr.kill()
+            out, _ = pr.communicate()
+        outs.append((pr.returncode, out))
+    (rc0, out0), (rc1, out1) = outs
+    assert rc1 == 5, out1[-2000:]
+    assert rc0 == 0, out0[-2000:]
+    assert "rank0 step 0 done" in out0
+    assert "rank0 PEER_FAILURE step=1 missing=[1]" in out0, out0[-2000:]
