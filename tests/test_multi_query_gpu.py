@@ -106,3 +106,15 @@ def test_large_group_many_query_tokens(cuda_device):
                                causal=bool(causal))
         out = run_abi(inp, q, causal, cuda_device)
         assert_parity(out, ref, what=f"Sq=8 g=8 causal={causal}")
+
+
+def test_sixteen_query_tokens_many_row_groups(cuda_device):
+    """g = 8 and Sq = 16: 128 query rows per KV head, 16 row groups per unit."""
+    Sq, Hq, Hkv, P = 16, 32, 4, 16
+    lens = [5, 16, 17, 900]
+    inp, q = multi_query_case(len(lens), Sq, Hq, Hkv, P, lens, seed=23)
+    for causal in (0, 1):
+        ref = paged_decode_ref(q, inp.k, inp.v, inp.block_table, inp.seq_lens,
+                               causal=bool(causal))
+        out = run_v2(inp, q, causal, cuda_device)
+        assert_parity(out, ref, edge=True, what=f"Sq=16 causal={causal}")

@@ -128,7 +128,7 @@ def test_c5_full_size_sampled_rows_and_page_permutation(cuda_device):
 
 @pytest.mark.parametrize("P", [16, 32, 64, 128])
 @pytest.mark.parametrize("Hq,Hkv", [(32, 8), (32, 4), (28, 4), (8, 8), (16, 1), (64, 2),
-                                    (24, 3), (6, 2)])
+                                    (24, 3), (6, 2), (64, 1)])
 def test_edge_lengths_poisoned(P, Hq, Hkv, cuda_device):
     lens = [1, 2, 15, 16, 17, P - 1, P, P + 1, 2 * P + 3, 100, 1000, 31, 33]
     width = max((L + P - 1) // P for L in lens) + 2
