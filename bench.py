@@ -19,6 +19,8 @@ roofline   achieved = algorithmic bytes per launch / mean launch time, against t
 cpu_baseline  the CPU oracle (fp32 PyTorch paged attention, all host threads) on a bounded
            sample of the same workload, rank 0 at N=1 only.
 
+scaling_reference  (N=1 lines) c5, the workload the N>1 runs shard, on this one GPU.
+
 --kv fp8 runs the same workload with e4m3 KV pages (per-KV-head scales; an extension,
 the reference's pools are bf16): value counts the e4m3 bytes; no e2e or CPU leg.
 
@@ -53,6 +55,8 @@ def parse():
     ap.add_argument("--config", default=None, choices=["c1", "c2", "c3", "c4", "c5"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-scaling-ref", action="store_true",
+                    help="skip the single-GPU c5 measurement added to N=1 lines")
     ap.add_argument("--e2e-host-budget-gb", type=float, default=8.0)
     ap.add_argument("--out", default=None, help="also append the JSON line to this file")
     ap.add_argument("--profile", type=int, default=0,
@@ -425,6 +429,10 @@ def main():
             ms, kvb = e2e.pop("_ms"), e2e.pop("_kv")
             e2e["value"] = round(kvb / (ms / 1e3) / 1e9, 3)
 
+    scaling_ref = None
+    if world == 1 and not args.no_scaling_ref and not fp8 and name != "c5":
+        scaling_ref = scaling_reference(dev, stream)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and not fp8:
         cpu = time_cpu_oracle(name, budget_s=10.0)
@@ -458,6 +466,8 @@ def main():
         }
         if allgather is not None:
             line["allgather"] = allgather
+        if scaling_ref is not None:
+            line["scaling_reference"] = scaling_ref
         if cpu is not None:
             line["cpu_baseline"] = cpu
         s = json.dumps(line)
@@ -488,6 +498,41 @@ def profile_calls(args, world):
     torch.cuda.synchronize(dev)
     ops.check_device_error(ws, dev)
     print(json.dumps({"profile_calls": args.profile, "workload": name, "kv": args.kv}))
+
+
+def scaling_reference(dev, stream, steps=10):
+    """The multi-GPU workload (c5, all KV heads) on this one GPU: the N=1 point of the
+    scaling series that bench.py runs at N>1 (device time, same method as `value`)."""
+    import torch
+    from mx_flash_attn_kernel_opt__b200 import _lib, inputs, ops
+    inp = inputs.baseline_config("c5", device=dev)
+    out = torch.empty_like(inp.q)
+    ws = ops.workspace_for(inp.batch, inp.num_heads, inp.num_heads_k, 128, inp.page_size, dev)
+    vp = ctypes.c_void_p
+    args = (vp(inp.q.data_ptr()), vp(inp.k.data_ptr()), vp(inp.v.data_ptr()), vp(out.data_ptr()),
+            vp(inp.seq_lens.data_ptr()), vp(inp.block_table.data_ptr()), inp.batch,
+            inp.num_heads, inp.num_heads_k, 128, inp.page_size, inp.num_pages,
+            inp.block_table.stride(0), 0, ctypes.c_float(inp.scale), vp(ws.data_ptr()),
+            ws.numel(), vp(stream.cuda_stream))
+    L = _lib.lib()
+    for _ in range(3):
+        _lib.check(L.pgqa_decode_v1(*args), "pgqa_decode_v1")
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        L.pgqa_decode_v1(*args)
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    ops.check_device_error(ws, dev)
+    per = e0.elapsed_time(e1) / 1e3 / steps
+    kvb = inp.kv_bytes()
+    del inp, out
+    torch.cuda.empty_cache()
+    return {"workload": describe("c5", 1), "n_gpus": 1, "steps": steps,
+            "us_per_call": round(per * 1e6, 2), "value": round(kvb / per / 1e9, 3), "unit": "GB/s",
+            "note": "bench.py at N>1 runs this workload sharded by KV head; read scaling "
+                    "against this value (the N=1 line's `value` is the c2 headline)"}
 
 
 def e2e_measure(inp, dev, stream, steps, budget_gb, world):
