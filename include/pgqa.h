@@ -186,12 +186,14 @@ int pgqa_decode_noalloc(const void* q, const void* k_cache, const void* v_cache,
 
 /* Bytes of workspace pgqa_decode_v1 needs for this shape on the current device
  * (no counterpart in the reference, whose workspace is a hidden static buffer,
- * submission_clean.cu:478-491).  Returns 0 on invalid shapes. */
+ * submission_clean.cu:478-491).  Returns 0 on invalid or unsupported shapes;
+ * pgqa_last_status() then holds the reason. */
 size_t pgqa_workspace_size(int64_t batch_size, int64_t num_heads, int64_t num_heads_k,
                            int64_t headdim, int64_t page_size);
 
 /* Workspace bytes for pgqa_decode_v2 with seqlen_q query tokens (no counterpart in
- * the reference).  Returns 0 on invalid shapes. */
+ * the reference).  Returns 0 on invalid or unsupported shapes; pgqa_last_status() then
+ * holds the reason. */
 size_t pgqa_workspace_size_v2(int64_t batch_size, int64_t seqlen_q, int64_t num_heads,
                               int64_t num_heads_k, int64_t headdim, int64_t page_size);
 

@@ -1527,8 +1527,9 @@ static size_t workspace_size_impl(int64_t batch_size, int64_t seqlen_q, int64_t 
         cudaGetLastError();
     }
     pgqa_plan plan;
-    if (make_plan_impl(batch_size, seqlen_q, num_heads, num_heads_k, headdim, page_size, sms, optin,
-                       &plan) != PGQA_OK)
+    // the reason for a 0 (bad or unsupported shape) is left for pgqa_last_status()
+    if (set_status(make_plan_impl(batch_size, seqlen_q, num_heads, num_heads_k, headdim,
+                                  page_size, sms, optin, &plan)) != PGQA_OK)
         return 0;
     return (size_t)plan.workspace_bytes;
 }

@@ -39,7 +39,7 @@ def workspace_for(batch_size, num_heads, num_heads_k, headdim, page_size, device
         need = L.pgqa_workspace_size_v2(batch_size, seqlen_q, num_heads, num_heads_k, headdim,
                                         page_size)
     if need == 0:
-        raise PgqaError(2, "pgqa_workspace_size_v2")
+        raise PgqaError(L.pgqa_last_status() or 2, "pgqa_workspace_size_v2")
     ws = _workspaces.get(dev.index)
     if ws is None or ws.numel() < need:
         ws = torch.zeros(max(need, 1 << 20), dtype=torch.uint8, device=dev)

@@ -131,5 +131,9 @@ def test_workspace_size_is_zero_for_invalid_shapes():
     assert L.pgqa_workspace_size(0, 32, 8, 128, 16) == 0
     assert L.pgqa_workspace_size(4, 32, 8, 128, 16) > 0
     assert L.pgqa_workspace_size_v2(4, 0, 32, 8, 128, 16) == 0
+    assert L.pgqa_last_status() == 2
+    # a batch whose length prefix does not fit in shared memory: unsupported, not bad
+    assert L.pgqa_workspace_size(40000, 8, 2, 128, 16) == 0
+    assert L.pgqa_last_status() == 3
     # more query tokens -> more row groups per KV head -> more arrival counters
     assert L.pgqa_workspace_size_v2(4, 4, 32, 8, 128, 16) > L.pgqa_workspace_size(4, 32, 8, 128, 16)

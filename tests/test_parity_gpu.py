@@ -264,3 +264,31 @@ def test_undersized_or_misaligned_workspace_is_refused(cuda_device):
     assert e.value.status == 4
     torch.cuda.synchronize(cuda_device)
     assert bool((out == 7.0).all())
+
+
+def test_large_batch_prefix_table(cuda_device):
+    """B = 8000 short sequences: every CTA scans a long length table (31 per thread)."""
+    g = torch.Generator().manual_seed(77)
+    lens = torch.randint(1, 40, (8000,), generator=g).tolist()
+    inp = inputs.custom_case(len(lens), 8, 2, 16, lens, seed=78)
+    out = run_v1(inp, cuda_device)
+    rows = list(range(0, 8000, 97))
+    ref = paged_decode_ref(inp.q, inp.k, inp.v, inp.block_table, inp.seq_lens, rows=rows)
+    assert_parity(out[rows], ref[rows], what="B=8000")
+    f8 = inputs.to_fp8(inp)
+    d8 = f8.to(cuda_device)
+    out8 = pgqa.decode(d8.q, d8.k, d8.v, d8.block_table, d8.seq_lens, k_scale=d8.k_scale,
+                       v_scale=d8.v_scale)
+    torch.cuda.synchronize(cuda_device)
+    from oracle import paged_decode_fp8_ref
+    kd = f8.k.float() * f8.k_scale.view(1, 1, -1, 1)
+    vd = f8.v.float() * f8.v_scale.view(1, 1, -1, 1)
+    ref8 = paged_decode_ref(f8.q, kd, vd, f8.block_table, f8.seq_lens, rows=rows)
+    assert_parity(out8[rows], ref8[rows], what="B=8000 fp8")
+
+
+def test_batch_beyond_prefix_table_is_refused(cuda_device):
+    inp = inputs.custom_case(40000, 8, 2, 16, [1] * 40000, seed=79).to(cuda_device)
+    with pytest.raises(pgqa.PgqaError) as e:
+        pgqa.decode(inp.q, inp.k, inp.v, inp.block_table, inp.seq_lens)
+    assert e.value.status == 3
