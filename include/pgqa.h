@@ -221,11 +221,13 @@ typedef struct pgqa_plan {
     int32_t warps_per_cta;    /* streaming warps per CTA                              */
     int32_t stages;           /* TMA ring depth per warp (16-token stages)            */
     int32_t min_chunks_per_warp; /* lower bound on work per active warp (chunks)      */
-    int32_t head_groups;      /* query-head groups of <= 8 per KV head               */
-    int32_t units_per_seq;    /* num_heads_k * head_groups                            */
+    int32_t head_groups;      /* groups of <= 8 query rows per KV head               */
+    int32_t units_per_seq;    /* num_heads_k * ceil(head_groups / groups_per_unit)    */
     int32_t smem_bytes;       /* dynamic shared memory per CTA                        */
     int32_t status;           /* PGQA_OK or why the shape cannot run                  */
     int64_t workspace_bytes;  /* pgqa_workspace_size for this shape                   */
+    int32_t groups_per_unit;  /* row groups one warp carries over each K/V tile (1, 2) */
+    int32_t reserved;
 } pgqa_plan;
 
 /* Fill *plan for a shape on a device with `num_sms` SMs and `smem_per_block_optin`

@@ -28,6 +28,8 @@ class PgqaPlan(ctypes.Structure):
         ("smem_bytes", ctypes.c_int32),
         ("status", ctypes.c_int32),
         ("workspace_bytes", ctypes.c_int64),
+        ("groups_per_unit", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
     ]
 
     def as_dict(self):

@@ -76,11 +76,13 @@ struct DecodeParams {
     __nv_bfloat16* out;
     const int32_t* seq_lens;
     const int32_t* block_table;
-    float* rec_o;        // [2 * grid][8 M tiles][32 lanes] float4 (O^T fragments)
-    float* rec_lse;      // [2 * grid][8 M tiles][8 heads]
-    int32_t* counters;   // [B * U][8 M tiles] arrival counters
+    float* rec_o;        // [2 * grid * NG][8 M tiles][32 lanes] float4 (O^T fragments)
+    float* rec_lse;      // [2 * grid * NG][8 M tiles][8 heads]
+    int32_t* counters;   // [B * U * NG][8 M tiles] arrival counters
     int32_t* err;        // device error word
-    int32_t B, Hq, Hkv, g, n_hg, U;
+    // n_hg groups of 8 query rows per KV head; a unit carries NG of them (n_w units per
+    // KV head, U = Hkv * n_w per sequence): row group hg = w * NG + grp
+    int32_t B, Hq, Hkv, g, n_hg, n_w, U;
     int32_t Sq;      // query tokens per sequence
     int32_t rows;    // query rows per KV head = g * Sq (row r: head r / Sq, token r % Sq)
     int32_t causal;  // query token i sees keys [0, L - Sq + i] instead of [0, L)
@@ -253,20 +255,22 @@ struct PairMerge {
  * KV8 = true: e4m3 pools, 4 KB stages (one 128-byte box each for K and V); the fp8
  * bytes are converted exactly to f16 after ldmatrix and multiplied with f16 MMAs
  * (q rounded to f16 after an exact per-row power-of-two rescale; P in f16). */
-template <int W, int S, bool MQ, bool KV8>
+template <int W, int S, bool MQ, bool KV8, int NG>
 __global__ void __launch_bounds__(W * 32, 1)
 pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
                    const __grid_constant__ CUtensorMap vmap, const DecodeParams p) {
     constexpr int NT = W * 32;
     constexpr int kStage = KV8 ? kStageBytesKv8 : kStageBytes;
     constexpr int kVOff = KV8 ? kHalfBytes : 2 * kHalfBytes;  // V's offset inside a stage
-    // FP8: a warp's first cut unit goes straight to its own shared-memory slot when it
-    // completes (frees 32 registers for more warps); bf16 keeps it in registers.
-    constexpr bool kEarlyStash = KV8;
-    constexpr int kMiscInts = 32 + 4 * W;  // warp sums [32] + parked keys int2[2W]
-    static_assert((kEarlyStash ? 1 : 2) * sizeof(Stash) <= (size_t)S * kStage,
+    // A warp's first cut unit goes straight to its own shared-memory slots when it
+    // completes (FP8: frees 32 registers; NG > 1: its NG states would not fit in
+    // registers); bf16 with NG = 1 keeps it in registers.
+    constexpr bool kEarlyStash = KV8 || NG > 1;
+    constexpr int kStates = 2 * NG;           // parked states per warp (first, last) x groups
+    constexpr int kMiscInts = 32 + 2 * W * kStates;  // warp sums [32] + parked keys int2
+    static_assert((kEarlyStash ? NG : 2) * sizeof(Stash) <= (size_t)S * kStage,
                   "the states a warp parks in its ring must fit in it");
-    static_assert(2 * W <= 32, "parked states are scanned one per lane");
+    static_assert(W * kStates <= 32, "parked states are scanned one per lane");
     extern __shared__ uint8_t smem_raw[];
     // 128-byte TMA swizzle needs 1024-byte aligned stages (shared-window offset).
     uint8_t* smem = smem_raw + ((1024u - (ptx::smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -274,7 +278,7 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
     uint64_t* bars = reinterpret_cast<uint64_t*>(ring + W * S * kStage);   // W*S
     int32_t* misc = reinterpret_cast<int32_t*>(bars + W * S);               // kMiscInts
     uint32_t* pre = reinterpret_cast<uint32_t*>(misc + kMiscInts);          // B+1
-    // early stash slots (kEarlyStash): W x Stash after the prefix table, 16-byte aligned
+    // early stash slots (kEarlyStash): W x NG Stash after the prefix table, 16-byte aligned
     const uint32_t early_base = (ptx::smem_u32(pre + p.B + 1) + 15u) & ~15u;
 
     const int tid = threadIdx.x;
@@ -350,13 +354,13 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
     const uint32_t bar_base = ptx::smem_u32(bars);
     const uint64_t pol = ptx::policy_evict_first();
 
-    /* Per-warp streaming state kept until the CTA-level merge. */
+    /* Per-warp streaming state kept until the CTA-level merge (per row group grp). */
     bool have_first = false, have_last = false;
     Cursor first_u{}, last_u{};
-    float fo[8][4];
+    float fo[8][4];                 // first cut unit (NG = 1, bf16 only)
     float flse[2] = {0.f, 0.f};
-    float o[8][4];
-    float m2[2], l2[2];
+    float o[NG][8][4];
+    float m2[NG][2], l2[NG][2];
     bool aborted = false;
 
     if (warp < wa) {
@@ -374,7 +378,7 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
         // (no division per chunk: chunks are 16-token aligned and P is a multiple of 16)
         int32_t ipage = (ic.c * kChunkTokens) / P;
         int32_t ioff = ic.c * kChunkTokens - ipage * P;
-        int32_t ikvh = ic.j / p.n_hg;
+        int32_t ikvh = ic.j / p.n_w;
 
         auto issue_next = [&]() {
             const int32_t page = ipage;
@@ -415,7 +419,7 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
                 if (ic.c == 0) {  // a new unit starts at its first chunk
                     ipage = 0;
                     ioff = 0;
-                    ikvh = (p.n_hg == 1) ? ic.j : ic.j / p.n_hg;
+                    ikvh = (p.n_w == 1) ? ic.j : ic.j / p.n_w;
                 } else if ((ioff += kChunkTokens) == P) {
                     ioff = 0;
                     ++ipage;
@@ -426,25 +430,36 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
         const int64_t prologue = ntot < S ? ntot : S;
         for (int64_t k = 0; k < prologue; ++k) issue_next();
 
-        uint32_t qf[16];
-        int nh_valid = 0;
-        int32_t limA = 0, limB = 0;  // keys visible to this lane's two columns (rows)
+        uint32_t qf[NG][16];
+        int nh_valid[NG];       // valid rows of each row group (<= 0: an empty group)
+        int32_t limA[NG], limB[NG];  // keys visible to this lane's two columns (rows)
         // score multipliers of this lane's two columns and the V factor (FP8 pools)
-        float mulA = p.scale_log2, mulB = p.scale_log2, vsc = 1.f;
+        float mulA[NG], mulB[NG], vsc = 1.f;
+#pragma unroll
+        for (int gr = 0; gr < NG; ++gr) { mulA[gr] = p.scale_log2; mulB[gr] = p.scale_log2; }
         auto load_q = [&](const Cursor& cu) {
-            const int32_t kvh = cu.j / p.n_hg;
-            const int32_t hg = cu.j - kvh * p.n_hg;
-            nh_valid = min(kHeadsPerGroup, p.rows - hg * kHeadsPerGroup);
-            limA = row_limit<MQ>(p, hg * kHeadsPerGroup + 2 * tig, cu.L);
-            limB = row_limit<MQ>(p, hg * kHeadsPerGroup + 2 * tig + 1, cu.L);
+            const int32_t kvh = cu.j / p.n_w;
+            const int32_t wg = cu.j - kvh * p.n_w;
             if (KV8) {
-                /* qf[4m + 2hh + j] = f16 pair q[32m + 16hh + 4tig + 2j + {0,1}] of row gid,
-                 * the d order of the converted K fragments.  The row is scaled by 2^e
+                const float ks = p.k_scale ? __ldg(p.k_scale + kvh) : 1.f;
+                vsc = p.v_scale ? __ldg(p.v_scale + kvh) : 1.f;
+#pragma unroll
+                for (int gr = 0; gr < NG; ++gr) { mulA[gr] = p.scale_log2 * ks; mulB[gr] = mulA[gr]; }
+            }
+#pragma unroll
+            for (int gr = 0; gr < NG; ++gr) {
+            const int32_t hg = wg * NG + gr;
+            nh_valid[gr] = min(kHeadsPerGroup, p.rows - hg * kHeadsPerGroup);
+            limA[gr] = row_limit<MQ>(p, hg * kHeadsPerGroup + 2 * tig, cu.L);
+            limB[gr] = row_limit<MQ>(p, hg * kHeadsPerGroup + 2 * tig + 1, cu.L);
+            if (KV8) {
+                /* qf[gr][4m + 2hh + j] = f16 pair q[32m + 16hh + 4tig + 2j + {0,1}] of row
+                 * gid, the d order of the converted K fragments.  The row is scaled by 2^e
                  * (exact) so that its largest |q| lies in [2^14, 2^15): f16 then keeps all
                  * of bf16's precision without overflow; 2^-e goes into the score
                  * multiplier of that column. */
                 float qv[32];
-                if (gid < nh_valid) {
+                if (gid < nh_valid[gr]) {
                     const __nv_bfloat16* qp = p.q + row_offset<MQ>(p, cu.b, kvh, hg * kHeadsPerGroup + gid);
 #pragma unroll
                     for (int k = 0; k < 8; ++k) {
@@ -468,29 +483,31 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
                 const float up = __uint_as_float((uint32_t)(e + 127) << 23);
                 const float down = __uint_as_float((uint32_t)(127 - e) << 23);
 #pragma unroll
-                for (int i = 0; i < 16; ++i) qf[i] = ptx::pack_f16x2(qv[2 * i] * up, qv[2 * i + 1] * up);
-                const float ks = p.k_scale ? __ldg(p.k_scale + kvh) : 1.f;
-                vsc = p.v_scale ? __ldg(p.v_scale + kvh) : 1.f;
-                mulA = p.scale_log2 * ks * __shfl_sync(0xffffffffu, down, 8 * tig);
-                mulB = p.scale_log2 * ks * __shfl_sync(0xffffffffu, down, 8 * tig + 4);
-            } else if (gid < nh_valid) {
+                for (int i = 0; i < 16; ++i) qf[gr][i] = ptx::pack_f16x2(qv[2 * i] * up, qv[2 * i + 1] * up);
+                mulA[gr] *= __shfl_sync(0xffffffffu, down, 8 * tig);
+                mulB[gr] *= __shfl_sync(0xffffffffu, down, 8 * tig + 4);
+            } else if (gid < nh_valid[gr]) {
                 const uint32_t* qp = reinterpret_cast<const uint32_t*>(
                     p.q + row_offset<MQ>(p, cu.b, kvh, hg * kHeadsPerGroup + gid));
 #pragma unroll
                 for (int ks = 0; ks < 8; ++ks) {
-                    qf[2 * ks] = __ldg(qp + 8 * ks + tig);
-                    qf[2 * ks + 1] = __ldg(qp + 8 * ks + 4 + tig);
+                    qf[gr][2 * ks] = __ldg(qp + 8 * ks + tig);
+                    qf[gr][2 * ks + 1] = __ldg(qp + 8 * ks + 4 + tig);
                 }
             } else {
 #pragma unroll
-                for (int i = 0; i < 16; ++i) qf[i] = 0u;
+                for (int i = 0; i < 16; ++i) qf[gr][i] = 0u;
+            }
             }
         };
         auto reset_state = [&]() {
-            m2[0] = m2[1] = -INFINITY;
-            l2[0] = l2[1] = 0.f;
 #pragma unroll
-            for (int mt = 0; mt < 8; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+            for (int gr = 0; gr < NG; ++gr) {
+                m2[gr][0] = m2[gr][1] = -INFINITY;
+                l2[gr][0] = l2[gr][1] = 0.f;
+#pragma unroll
+                for (int mt = 0; mt < 8; ++mt) o[gr][mt][0] = o[gr][mt][1] = o[gr][mt][2] = o[gr][mt][3] = 0.f;
+            }
         };
 
         load_q(cc);
@@ -555,14 +572,18 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
                 __syncwarp();
             }
 
-            /* ---- S^T = K . Q^T : 16 tokens x 8 heads per chunk, K-dim = 128 ----
-             * s[c][0]: (t=gid, h=2tig) [1]: (gid, 2tig+1) [2]: (gid+8, 2tig) [3]: (gid+8, 2tig+1) */
-            float s[NC][4];
+            /* ---- S^T = K . Q^T : 16 tokens x 8 query rows per chunk and group, K-dim 128 ----
+             * s[c][gr][0]: (t=gid, h=2tig) [1]: (gid, 2tig+1) [2]: (gid+8, 2tig)
+             * [3]: (gid+8, 2tig+1); every K fragment serves the NG row groups. */
+            float s[NC][NG][4];
 #pragma unroll
             for (int c = 0; c < NC; ++c) {
                 const uint32_t sK = ring_base + (uint32_t)(warp * S + (int)((i + c) % S)) * kStage;
-                float sa[4] = {0.f, 0.f, 0.f, 0.f};
-                float sb[4] = {0.f, 0.f, 0.f, 0.f};
+                float sa[NG][4], sb[NG][4];
+#pragma unroll
+                for (int gr = 0; gr < NG; ++gr)
+#pragma unroll
+                    for (int r = 0; r < 4; ++r) sa[gr][r] = sb[gr][r] = 0.f;
                 if (KV8) {
                     /* One ldmatrix.x4 per 32 dims: matrices (t 0-7 | 8-15) x (16-byte units
                      * 2m | 2m+1); a lane gets 4 consecutive fp8 of one token, which convert
@@ -580,11 +601,19 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
                         ptx::e4m3x4_to_f16(r1, k1l, k1h);
                         ptx::e4m3x4_to_f16(r2, k2l, k2h);
                         ptx::e4m3x4_to_f16(r3, k3l, k3h);
-                        ptx::mma_f16_16816(sa, k0l, k1l, k0h, k1h, qf[4 * m], qf[4 * m + 1]);
-                        ptx::mma_f16_16816(sb, k2l, k3l, k2h, k3h, qf[4 * m + 2], qf[4 * m + 3]);
+#pragma unroll
+                        for (int gr = 0; gr < NG; ++gr) {
+                            ptx::mma_f16_16816(sa[gr], k0l, k1l, k0h, k1h, qf[gr][4 * m], qf[gr][4 * m + 1]);
+                            ptx::mma_f16_16816(sb[gr], k2l, k3l, k2h, k3h, qf[gr][4 * m + 2], qf[gr][4 * m + 3]);
+                        }
                     }
-                    s[c][0] = (sa[0] + sb[0]) * mulA; s[c][1] = (sa[1] + sb[1]) * mulB;
-                    s[c][2] = (sa[2] + sb[2]) * mulA; s[c][3] = (sa[3] + sb[3]) * mulB;
+#pragma unroll
+                    for (int gr = 0; gr < NG; ++gr) {
+                        s[c][gr][0] = (sa[gr][0] + sb[gr][0]) * mulA[gr];
+                        s[c][gr][1] = (sa[gr][1] + sb[gr][1]) * mulB[gr];
+                        s[c][gr][2] = (sa[gr][2] + sb[gr][2]) * mulA[gr];
+                        s[c][gr][3] = (sa[gr][3] + sb[gr][3]) * mulB[gr];
+                    }
                 } else {
 #pragma unroll
                     for (int ks = 0; ks < 8; ++ks) {
@@ -593,23 +622,31 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
                         const uint32_t addr = sK + half * kHalfBytes + tK * 128 + ((ch ^ mr) << 4);
                         uint32_t a0, a1, a2, a3;
                         ptx::ldsm_x4(addr, a0, a1, a2, a3);
-                        if (ks & 1) ptx::mma_bf16_16816(sb, a0, a1, a2, a3, qf[2 * ks], qf[2 * ks + 1]);
-                        else        ptx::mma_bf16_16816(sa, a0, a1, a2, a3, qf[2 * ks], qf[2 * ks + 1]);
+#pragma unroll
+                        for (int gr = 0; gr < NG; ++gr) {
+                            if (ks & 1) ptx::mma_bf16_16816(sb[gr], a0, a1, a2, a3, qf[gr][2 * ks], qf[gr][2 * ks + 1]);
+                            else        ptx::mma_bf16_16816(sa[gr], a0, a1, a2, a3, qf[gr][2 * ks], qf[gr][2 * ks + 1]);
+                        }
                     }
 #pragma unroll
-                    for (int r = 0; r < 4; ++r) s[c][r] = (sa[r] + sb[r]) * p.scale_log2;
+                    for (int gr = 0; gr < NG; ++gr)
+#pragma unroll
+                        for (int r = 0; r < 4; ++r) s[c][gr][r] = (sa[gr][r] + sb[gr][r]) * p.scale_log2;
                 }
-                if (MQ) {
-                    // keys past the row's limit (the sequence end, or the causal bound) -> -inf
-                    const int32_t t = (cc.c + c) * kChunkTokens + gid;
-                    s[c][0] = (t < limA) ? s[c][0] : -INFINITY;
-                    s[c][1] = (t < limB) ? s[c][1] : -INFINITY;
-                    s[c][2] = (t + 8 < limA) ? s[c][2] : -INFINITY;
-                    s[c][3] = (t + 8 < limB) ? s[c][3] : -INFINITY;
-                } else if (c == NC - 1 && nvalid < kChunkTokens) {
-                    // tokens past the sequence end -> -inf (every row sees the same keys)
-                    if (gid >= nvalid) { s[c][0] = -INFINITY; s[c][1] = -INFINITY; }
-                    if (gid + 8 >= nvalid) { s[c][2] = -INFINITY; s[c][3] = -INFINITY; }
+#pragma unroll
+                for (int gr = 0; gr < NG; ++gr) {
+                    if (MQ) {
+                        // keys past the row's limit (the sequence end, or the causal bound) -> -inf
+                        const int32_t t = (cc.c + c) * kChunkTokens + gid;
+                        s[c][gr][0] = (t < limA[gr]) ? s[c][gr][0] : -INFINITY;
+                        s[c][gr][1] = (t < limB[gr]) ? s[c][gr][1] : -INFINITY;
+                        s[c][gr][2] = (t + 8 < limA[gr]) ? s[c][gr][2] : -INFINITY;
+                        s[c][gr][3] = (t + 8 < limB[gr]) ? s[c][gr][3] : -INFINITY;
+                    } else if (c == NC - 1 && nvalid < kChunkTokens) {
+                        // tokens past the sequence end -> -inf (every row sees the same keys)
+                        if (gid >= nvalid) { s[c][gr][0] = -INFINITY; s[c][gr][1] = -INFINITY; }
+                        if (gid + 8 >= nvalid) { s[c][gr][2] = -INFINITY; s[c][gr][3] = -INFINITY; }
+                    }
                 }
             }
 
@@ -618,51 +655,65 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
              * scores exceeds it by more than kLazyLog2, so p <= 2^kLazyLog2 (fine in f16 /
              * bf16 and fp32).  o and l share the reference, so the result is the same; the
              * column reduction and the rescale of o and l run only when a lane votes. */
-            float mxA = fmaxf(s[0][0], s[0][2]);
-            float mxB = fmaxf(s[0][1], s[0][3]);
+            float mxA[NG], mxB[NG];
+            bool vote = false;
 #pragma unroll
-            for (int c = 1; c < NC; ++c) {
-                mxA = fmaxf(mxA, fmaxf(s[c][0], s[c][2]));
-                mxB = fmaxf(mxB, fmaxf(s[c][1], s[c][3]));
-            }
-            if (__any_sync(0xffffffffu, mxA > m2[0] + kLazyLog2 || mxB > m2[1] + kLazyLog2)) {
+            for (int gr = 0; gr < NG; ++gr) {
+                mxA[gr] = fmaxf(s[0][gr][0], s[0][gr][2]);
+                mxB[gr] = fmaxf(s[0][gr][1], s[0][gr][3]);
 #pragma unroll
-                for (int off = 4; off < 32; off <<= 1) {
-                    mxA = fmaxf(mxA, __shfl_xor_sync(0xffffffffu, mxA, off));
-                    mxB = fmaxf(mxB, __shfl_xor_sync(0xffffffffu, mxB, off));
+                for (int c = 1; c < NC; ++c) {
+                    mxA[gr] = fmaxf(mxA[gr], fmaxf(s[c][gr][0], s[c][gr][2]));
+                    mxB[gr] = fmaxf(mxB[gr], fmaxf(s[c][gr][1], s[c][gr][3]));
                 }
-                const float mnA = fmaxf(m2[0], mxA);
-                const float mnB = fmaxf(m2[1], mxB);
-                // a row with no visible key yet keeps max -inf: rescale against 0 instead
-                const float zA = (MQ && mnA == -INFINITY) ? 0.f : mnA;
-                const float zB = (MQ && mnB == -INFINITY) ? 0.f : mnB;
-                const float alA = ptx::ex2(m2[0] - zA);
-                const float alB = ptx::ex2(m2[1] - zB);
-                m2[0] = mnA;
-                m2[1] = mnB;
-                l2[0] *= alA;
-                l2[1] *= alB;
+                vote = vote || mxA[gr] > m2[gr][0] + kLazyLog2 || mxB[gr] > m2[gr][1] + kLazyLog2;
+            }
+            if (__any_sync(0xffffffffu, vote)) {
 #pragma unroll
-                for (int mt = 0; mt < 8; ++mt) {
-                    o[mt][0] *= alA; o[mt][1] *= alB; o[mt][2] *= alA; o[mt][3] *= alB;
+                for (int gr = 0; gr < NG; ++gr) {
+#pragma unroll
+                    for (int off = 4; off < 32; off <<= 1) {
+                        mxA[gr] = fmaxf(mxA[gr], __shfl_xor_sync(0xffffffffu, mxA[gr], off));
+                        mxB[gr] = fmaxf(mxB[gr], __shfl_xor_sync(0xffffffffu, mxB[gr], off));
+                    }
+                    const float mnA = fmaxf(m2[gr][0], mxA[gr]);
+                    const float mnB = fmaxf(m2[gr][1], mxB[gr]);
+                    // a row with no visible key yet keeps max -inf: rescale against 0 instead
+                    const float zA = (MQ && mnA == -INFINITY) ? 0.f : mnA;
+                    const float zB = (MQ && mnB == -INFINITY) ? 0.f : mnB;
+                    const float alA = ptx::ex2(m2[gr][0] - zA);
+                    const float alB = ptx::ex2(m2[gr][1] - zB);
+                    m2[gr][0] = mnA;
+                    m2[gr][1] = mnB;
+                    l2[gr][0] *= alA;
+                    l2[gr][1] *= alB;
+#pragma unroll
+                    for (int mt = 0; mt < 8; ++mt) {
+                        o[gr][mt][0] *= alA; o[gr][mt][1] *= alB; o[gr][mt][2] *= alA; o[gr][mt][3] *= alB;
+                    }
                 }
             }
-            // (with one query token every chunk holds a visible key for every row)
-            const float bsA = (MQ && m2[0] == -INFINITY) ? 0.f : m2[0];
-            const float bsB = (MQ && m2[1] == -INFINITY) ? 0.f : m2[1];
 #pragma unroll
             for (int c = 0; c < NC; ++c) {
-                const float p0 = ptx::ex2(s[c][0] - bsA);
-                const float p1 = ptx::ex2(s[c][1] - bsB);
-                const float p2 = ptx::ex2(s[c][2] - bsA);
-                const float p3 = ptx::ex2(s[c][3] - bsB);
-                l2[0] += p0 + p2;
-                l2[1] += p1 + p3;
-                /* P^T (tokens x heads) C-fragment -> B-fragment of the PV MMA. */
-                const uint32_t pb0 = ptx::movmatrix_t(KV8 ? ptx::pack_f16x2(p0, p1) : ptx::pack_bf16x2(p0, p1));
-                const uint32_t pb1 = ptx::movmatrix_t(KV8 ? ptx::pack_f16x2(p2, p3) : ptx::pack_bf16x2(p2, p3));
+                uint32_t pb[NG][2];
+#pragma unroll
+                for (int gr = 0; gr < NG; ++gr) {
+                    // (with one query token every chunk holds a visible key for every row)
+                    const float bsA = (MQ && m2[gr][0] == -INFINITY) ? 0.f : m2[gr][0];
+                    const float bsB = (MQ && m2[gr][1] == -INFINITY) ? 0.f : m2[gr][1];
+                    const float p0 = ptx::ex2(s[c][gr][0] - bsA);
+                    const float p1 = ptx::ex2(s[c][gr][1] - bsB);
+                    const float p2 = ptx::ex2(s[c][gr][2] - bsA);
+                    const float p3 = ptx::ex2(s[c][gr][3] - bsB);
+                    l2[gr][0] += p0 + p2;
+                    l2[gr][1] += p1 + p3;
+                    /* P^T (tokens x heads) C-fragment -> B-fragment of the PV MMA. */
+                    pb[gr][0] = ptx::movmatrix_t(KV8 ? ptx::pack_f16x2(p0, p1) : ptx::pack_bf16x2(p0, p1));
+                    pb[gr][1] = ptx::movmatrix_t(KV8 ? ptx::pack_f16x2(p2, p3) : ptx::pack_bf16x2(p2, p3));
+                }
 
-                /* ---- O^T += V^T . P^T : 128 dims (8 M tiles) x 8 heads, K-dim = 16 tokens ---- */
+                /* ---- O^T += V^T . P^T : 128 dims (8 M tiles) x 8 rows, K-dim = 16 tokens;
+                 * every V fragment serves the NG row groups ---- */
                 const uint32_t sV = ring_base + (uint32_t)(warp * S + (int)((i + c) % S)) * kStage + kVOff;
                 if (KV8) {
                     /* ldmatrix.trans on byte pairs: a lane gets V[2tig][d0], V[2tig][d0+1],
@@ -678,8 +729,11 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
                         uint32_t x[4], y[4];
 #pragma unroll
                         for (int k = 0; k < 4; ++k) ptx::e4m3x4_to_f16(ptx::prmt(r[k], r[k], 0x3120u), x[k], y[k]);
-                        ptx::mma_f16_16816(o[2 * c2], x[0], y[0], x[1], y[1], pb0, pb1);
-                        ptx::mma_f16_16816(o[2 * c2 + 1], x[2], y[2], x[3], y[3], pb0, pb1);
+#pragma unroll
+                        for (int gr = 0; gr < NG; ++gr) {
+                            ptx::mma_f16_16816(o[gr][2 * c2], x[0], y[0], x[1], y[1], pb[gr][0], pb[gr][1]);
+                            ptx::mma_f16_16816(o[gr][2 * c2 + 1], x[2], y[2], x[3], y[3], pb[gr][0], pb[gr][1]);
+                        }
                     }
                 } else {
 #pragma unroll
@@ -689,7 +743,9 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
                         const uint32_t addr = sV + half * kHalfBytes + tV * 128 + ((ch ^ mr) << 4);
                         uint32_t a0, a1, a2, a3;
                         ptx::ldsm_x4_t(addr, a0, a1, a2, a3);
-                        ptx::mma_bf16_16816(o[mt], a0, a1, a2, a3, pb0, pb1);
+#pragma unroll
+                        for (int gr = 0; gr < NG; ++gr)
+                            ptx::mma_bf16_16816(o[gr][mt], a0, a1, a2, a3, pb[gr][0], pb[gr][1]);
                     }
                 }
             }
@@ -701,60 +757,66 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
             cc.c += NC - 1;  // the cursor now names the step's last chunk
             const bool last_of_warp = (i + NC - 1 == ntot - 1);
             if (last_of_unit || last_of_warp) {
-                /* ---- finish this warp's part of the unit ---- */
-                float lA = l2[0], lB = l2[1];
-#pragma unroll
-                for (int off = 4; off < 32; off <<= 1) {
-                    lA += __shfl_xor_sync(0xffffffffu, lA, off);
-                    lB += __shfl_xor_sync(0xffffffffu, lB, off);
-                }
-                // a row with no visible key gives 0 (only with several query tokens);
-                // FP8 pools fold V's dequantisation factor in here
-                const float invA = (!MQ || lA > 0.f) ? (KV8 ? vsc : 1.f) / lA : 0.f;
-                const float invB = (!MQ || lB > 0.f) ? (KV8 ? vsc : 1.f) / lB : 0.f;
+                /* ---- finish this warp's part of the unit, one row group at a time ---- */
                 const bool full = unit_start_seen && last_of_unit;
-                if (full) {
-                    const int32_t kvh = cc.j / p.n_hg;
-                    const int32_t hg = cc.j - kvh * p.n_hg;
-                    __nv_bfloat16* orow =
-                        p.out + row_offset<MQ>(p, cc.b, kvh, hg * kHeadsPerGroup + min(gid, nh_valid - 1));
 #pragma unroll
-                    for (int mt = 0; mt < 8; ++mt)
-                        store_tile<KV8>(orow, o[mt][0], o[mt][1], o[mt][2], o[mt][3], invA, invB, mt,
-                                        tig, gid < nh_valid);
-                } else {
-                    const float lseA = m2[0] + ptx::lg2(lA);
-                    const float lseB = m2[1] + ptx::lg2(lB);
-                    if (units_done == 0) {
-                        if (kEarlyStash) {
-                            const uint32_t a0 = early_base + (uint32_t)(warp * sizeof(Stash));
+                for (int gr = 0; gr < NG; ++gr) {
+                    float lA = l2[gr][0], lB = l2[gr][1];
+#pragma unroll
+                    for (int off = 4; off < 32; off <<= 1) {
+                        lA += __shfl_xor_sync(0xffffffffu, lA, off);
+                        lB += __shfl_xor_sync(0xffffffffu, lB, off);
+                    }
+                    // a row with no visible key gives 0 (only with several query tokens);
+                    // FP8 pools fold V's dequantisation factor in here
+                    const float invA = (!MQ || lA > 0.f) ? (KV8 ? vsc : 1.f) / lA : 0.f;
+                    const float invB = (!MQ || lB > 0.f) ? (KV8 ? vsc : 1.f) / lB : 0.f;
+                    if (full) {
+                        if (nh_valid[gr] > 0) {  // an empty group (rows past g * Sq) stores nothing
+                            const int32_t kvh = cc.j / p.n_w;
+                            const int32_t hg = (cc.j - kvh * p.n_w) * NG + gr;
+                            __nv_bfloat16* orow = p.out + row_offset<MQ>(
+                                p, cc.b, kvh, hg * kHeadsPerGroup + min(gid, nh_valid[gr] - 1));
 #pragma unroll
                             for (int mt = 0; mt < 8; ++mt)
-                                ptx::sts_f4(a0 + (mt * 32 + lane) * 16,
-                                            make_float4(o[mt][0] * invA, o[mt][1] * invB,
-                                                        o[mt][2] * invA, o[mt][3] * invB));
-                            if (gid == 0)
-                                ptx::sts_f2(a0 + offsetof(Stash, lse) + tig * 8, make_float2(lseA, lseB));
+                                store_tile<KV8>(orow, o[gr][mt][0], o[gr][mt][1], o[gr][mt][2],
+                                                o[gr][mt][3], invA, invB, mt, tig, gid < nh_valid[gr]);
+                        }
+                    } else {
+                        const float lseA = m2[gr][0] + ptx::lg2(lA);
+                        const float lseB = m2[gr][1] + ptx::lg2(lB);
+                        if (units_done == 0) {
+                            if (kEarlyStash) {
+                                const uint32_t a0 = early_base + (uint32_t)((warp * NG + gr) * sizeof(Stash));
+#pragma unroll
+                                for (int mt = 0; mt < 8; ++mt)
+                                    ptx::sts_f4(a0 + (mt * 32 + lane) * 16,
+                                                make_float4(o[gr][mt][0] * invA, o[gr][mt][1] * invB,
+                                                            o[gr][mt][2] * invA, o[gr][mt][3] * invB));
+                                if (gid == 0)
+                                    ptx::sts_f2(a0 + offsetof(Stash, lse) + tig * 8, make_float2(lseA, lseB));
+                            } else {
+#pragma unroll
+                                for (int mt = 0; mt < 8; ++mt) {
+                                    fo[mt][0] = o[0][mt][0] * invA; fo[mt][1] = o[0][mt][1] * invB;
+                                    fo[mt][2] = o[0][mt][2] * invA; fo[mt][3] = o[0][mt][3] * invB;
+                                }
+                                flse[0] = lseA; flse[1] = lseB;
+                            }
                         } else {
+                            // Only the warp's last unit can be cut at its end: keep it in place.
 #pragma unroll
                             for (int mt = 0; mt < 8; ++mt) {
-                                fo[mt][0] = o[mt][0] * invA; fo[mt][1] = o[mt][1] * invB;
-                                fo[mt][2] = o[mt][2] * invA; fo[mt][3] = o[mt][3] * invB;
+                                o[gr][mt][0] *= invA; o[gr][mt][1] *= invB;
+                                o[gr][mt][2] *= invA; o[gr][mt][3] *= invB;
                             }
-                            flse[0] = lseA; flse[1] = lseB;
+                            m2[gr][0] = lseA; m2[gr][1] = lseB;
                         }
-                        first_u = cc;
-                        have_first = true;
-                    } else {
-                        // Only the warp's last unit can be cut at its end: keep it in place.
-#pragma unroll
-                        for (int mt = 0; mt < 8; ++mt) {
-                            o[mt][0] *= invA; o[mt][1] *= invB; o[mt][2] *= invA; o[mt][3] *= invB;
-                        }
-                        m2[0] = lseA; m2[1] = lseB;
-                        last_u = cc;
-                        have_last = true;
                     }
+                }
+                if (!full) {
+                    if (units_done == 0) { first_u = cc; have_first = true; }
+                    else { last_u = cc; have_last = true; }
                 }
                 ++units_done;
                 if (!last_of_warp) {
@@ -785,36 +847,52 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
     ptx::griddep_launch_dependents();
 
     /* ---- park this warp's cut units in its own (now idle) ring: no TMA is in flight ----
-     * Parked state f = 2 * warp + slot lives at the start of warp `warp`'s ring (slot 0
-     * in the early-stash slot when kEarlyStash); its key (b, j), or (-1, -1) when empty,
-     * goes to a compact table for the run scan. */
+     * Parked state f = (2 * warp + slot) * NG + grp (slot 0: the warp's first cut unit,
+     * 1: its last; grp: row group) lives at the start of warp `warp`'s ring -- slot 0 in
+     * the early-stash slots when kEarlyStash.  Its key (b, unit * NG + grp), or (-1, -1)
+     * when empty, goes to a compact table for the run scan. */
     auto stash_addr = [&](int f) -> uint32_t {
-        if (kEarlyStash) {  // slot 0 in the early-stash slot, slot 1 at the ring's start
-            if (!(f & 1)) return early_base + (uint32_t)((f >> 1) * sizeof(Stash));
-            return ring_base + (uint32_t)((f >> 1) * S * kStage);
+        const int wf = f / (2 * NG), slot = (f / NG) & 1, gr = f % NG;
+        if (kEarlyStash) {  // slot 0 in the early-stash slots, slot 1 at the ring's start
+            if (slot == 0) return early_base + (uint32_t)((wf * NG + gr) * sizeof(Stash));
+            return ring_base + (uint32_t)(wf * S * kStage + gr * sizeof(Stash));
         }
-        return ring_base + (uint32_t)((f >> 1) * S * kStage) + (uint32_t)((f & 1) * sizeof(Stash));
+        return ring_base + (uint32_t)(wf * S * kStage) + (uint32_t)(slot * sizeof(Stash));
     };
-    const uint32_t keys_base = ptx::smem_u32(misc + 32);  // int2 keys[2W]
+    // a row group past g * Sq (the second group of an odd count) has no rows: no state
+    auto group_used = [&](const Cursor& cu, int gr) {
+        if (NG == 1) return true;  // a unit is one row group, always within the rows
+        return ((cu.j % p.n_w) * NG + gr) * kHeadsPerGroup < p.rows;
+    };
+    const uint32_t keys_base = ptx::smem_u32(misc + 32);  // int2 keys[2 W NG]
     {
         const bool v0 = (warp < wa) && have_first && !aborted;
         const bool v1 = (warp < wa) && have_last && !aborted;
-        const uint32_t a0 = stash_addr(2 * warp), a1 = stash_addr(2 * warp + 1);
         if (v0 && !kEarlyStash) {
+            const uint32_t a0 = stash_addr(2 * warp);
 #pragma unroll
             for (int mt = 0; mt < 8; ++mt)
                 ptx::sts_f4(a0 + (mt * 32 + lane) * 16, make_float4(fo[mt][0], fo[mt][1], fo[mt][2], fo[mt][3]));
             if (gid == 0) ptx::sts_f2(a0 + offsetof(Stash, lse) + tig * 8, make_float2(flse[0], flse[1]));
         }
-        if (v1) {
 #pragma unroll
-            for (int mt = 0; mt < 8; ++mt)
-                ptx::sts_f4(a1 + (mt * 32 + lane) * 16, make_float4(o[mt][0], o[mt][1], o[mt][2], o[mt][3]));
-            if (gid == 0) ptx::sts_f2(a1 + offsetof(Stash, lse) + tig * 8, make_float2(m2[0], m2[1]));
-        }
-        if (lane == 0) {
-            ptx::sts_i2(keys_base + (2 * warp) * 8, v0 ? make_int2(first_u.b, first_u.j) : make_int2(-1, -1));
-            ptx::sts_i2(keys_base + (2 * warp + 1) * 8, v1 ? make_int2(last_u.b, last_u.j) : make_int2(-1, -1));
+        for (int gr = 0; gr < NG; ++gr) {
+            if (v1) {
+                const uint32_t a1 = stash_addr((2 * warp + 1) * NG + gr);
+#pragma unroll
+                for (int mt = 0; mt < 8; ++mt)
+                    ptx::sts_f4(a1 + (mt * 32 + lane) * 16,
+                                make_float4(o[gr][mt][0], o[gr][mt][1], o[gr][mt][2], o[gr][mt][3]));
+                if (gid == 0) ptx::sts_f2(a1 + offsetof(Stash, lse) + tig * 8, make_float2(m2[gr][0], m2[gr][1]));
+            }
+            if (lane == 0) {
+                ptx::sts_i2(keys_base + ((2 * warp) * NG + gr) * 8,
+                            v0 && group_used(first_u, gr) ? make_int2(first_u.b, first_u.j * NG + gr)
+                                                          : make_int2(-1, -1));
+                ptx::sts_i2(keys_base + ((2 * warp + 1) * NG + gr) * 8,
+                            v1 && group_used(last_u, gr) ? make_int2(last_u.b, last_u.j * NG + gr)
+                                                         : make_int2(-1, -1));
+            }
         }
     }
     __syncthreads();
@@ -826,7 +904,7 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
      * counts arrivals per (unit, M tile); the warp that completes a tile merges it across
      * all CTAs' records.  Merges take the maximum first and select, never branch, on
      * membership, so every load of a pass is issued at once. */
-    constexpr int NF = 2 * W;
+    constexpr int NF = W * kStates;
     int2 key = make_int2(-1, -1);
     if (lane < NF) key = ptx::lds_i2(keys_base + lane * 8);
     const unsigned vmask = __ballot_sync(0xffffffffu, lane < NF && key.x >= 0);
@@ -838,41 +916,46 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
         const unsigned run = __ballot_sync(0xffffffffu, ((vmask >> lane) & 1u) && key.x == ub && key.y == uj);
         rem &= ~run;
 
+        const int32_t uu = uj / NG;        // the unit
+        const int gq = uj - uu * NG;         // its row group, the same for the whole run
         const int32_t n_u = (int32_t)(pre[ub + 1] - pre[ub]);
-        const int64_t ubeg = unit_begin(p, pre, ub, uj);
-        const int32_t kvh = uj / p.n_hg;
-        const int32_t hg = uj - kvh * p.n_hg;
+        const int64_t ubeg = unit_begin(p, pre, ub, uu);
+        const int32_t kvh = uu / p.n_w;
+        const int32_t hg = (uu - kvh * p.n_w) * NG + gq;
         const int nhv = min(kHeadsPerGroup, p.rows - hg * kHeadsPerGroup);
         const bool inside = (ubeg >= cs && ubeg + n_u <= ce);
         __nv_bfloat16* orow = p.out + row_offset<MQ>(p, ub, kvh, hg * kHeadsPerGroup + min(gid, nhv - 1));
+        // only states of row group gq can be in the run: f = fi * NG + gq
+        constexpr int NFG = NF / NG;
         for (int mt = warp; mt < 8; mt += W) {
-            float2 ls[NF];
-            float4 v[NF];
+            float2 ls[NFG];
+            float4 v[NFG];
 #pragma unroll
-            for (int f = 0; f < NF; ++f) {
-                ls[f] = ptx::lds_f2(stash_addr(f) + offsetof(Stash, lse) + tig * 8);
-                v[f] = ptx::lds_f4(stash_addr(f) + (mt * 32 + lane) * 16);
+            for (int fi = 0; fi < NFG; ++fi) {
+                const uint32_t sa = stash_addr(fi * NG + gq);
+                ls[fi] = ptx::lds_f2(sa + offsetof(Stash, lse) + tig * 8);
+                v[fi] = ptx::lds_f4(sa + (mt * 32 + lane) * 16);
             }
             float bA = -INFINITY, bB = -INFINITY;
 #pragma unroll
-            for (int f = 0; f < NF; ++f) {
-                const bool in = (run >> f) & 1u;
-                bA = in ? fmaxf(bA, ls[f].x) : bA;
-                bB = in ? fmaxf(bB, ls[f].y) : bB;
+            for (int fi = 0; fi < NFG; ++fi) {
+                const bool in = (run >> (fi * NG + gq)) & 1u;
+                bA = in ? fmaxf(bA, ls[fi].x) : bA;
+                bB = in ? fmaxf(bB, ls[fi].y) : bB;
             }
             float dA = 0.f, dB = 0.f, a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
             const float zA = (MQ && bA == -INFINITY) ? 0.f : bA;  // rows with no key: weight 0
             const float zB = (MQ && bB == -INFINITY) ? 0.f : bB;
 #pragma unroll
-            for (int f = 0; f < NF; ++f) {
-                const bool in = (run >> f) & 1u;
-                const float wA = ptx::ex2(ls[f].x - zA), wB = ptx::ex2(ls[f].y - zB);
+            for (int fi = 0; fi < NFG; ++fi) {
+                const bool in = (run >> (fi * NG + gq)) & 1u;
+                const float wA = ptx::ex2(ls[fi].x - zA), wB = ptx::ex2(ls[fi].y - zB);
                 dA = in ? dA + wA : dA;
                 dB = in ? dB + wB : dB;
-                a0 = in ? fmaf(wA, v[f].x, a0) : a0;
-                a1 = in ? fmaf(wB, v[f].y, a1) : a1;
-                a2 = in ? fmaf(wA, v[f].z, a2) : a2;
-                a3 = in ? fmaf(wB, v[f].w, a3) : a3;
+                a0 = in ? fmaf(wA, v[fi].x, a0) : a0;
+                a1 = in ? fmaf(wB, v[fi].y, a1) : a1;
+                a2 = in ? fmaf(wA, v[fi].z, a2) : a2;
+                a3 = in ? fmaf(wB, v[fi].w, a3) : a3;
             }
             const float invA = (!MQ || dA > 0.f) ? 1.f / dA : 0.f;
             const float invB = (!MQ || dB > 0.f) ? 1.f / dB : 0.f;
@@ -880,7 +963,7 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
                 store_tile<KV8>(orow, a0, a1, a2, a3, invA, invB, mt, tig, gid < nhv);
                 continue;
             }
-            const int64_t slot = record_slot(blockIdx.x, cs, ubeg);
+            const int64_t slot = record_slot(blockIdx.x, cs, ubeg) * NG + gq;
             reinterpret_cast<float4*>(p.rec_o)[(slot * 8 + mt) * 32 + lane] =
                 make_float4(a0 * invA, a1 * invB, a2 * invA, a3 * invB);
             if (gid == 0)
@@ -891,7 +974,7 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
             int last = 0;
             __syncwarp();  // the warp's record stores happen before lane 0's release
             if (lane == 0) {
-                int32_t* cnt = p.counters + ((int64_t)ub * p.U + uj) * 8 + mt;
+                int32_t* cnt = p.counters + (((int64_t)ub * p.U + uu) * NG + gq) * 8 + mt;
                 ptx::fence_acq_rel_gpu();  // release this CTA's record tile
                 const int32_t prev = ptx::atom_add_relaxed_gpu(cnt, 1);
                 if (prev == (int32_t)(c_last - c_first)) {
@@ -907,7 +990,7 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
             const int nrec = (int)(c_last - c_first + 1);
             // Record slots: CTA c_first holds the unit's head in slot 2c+1 unless its slice
             // starts exactly at the unit; every later CTA holds it in slot 2c.
-            const int64_t slot0 = record_slot(c_first, slice_begin(c_first, nct, T), ubeg);
+            const int64_t slot0 = record_slot(c_first, slice_begin(c_first, nct, T), ubeg) * NG + gq;
             PairMerge<MQ> g;
             g.init();
             for (int r0 = 0; r0 < nrec; r0 += 16) {
@@ -918,7 +1001,7 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
                     lse[u] = make_float2(-INFINITY, -INFINITY);
                     rv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
                     if (r0 + u < nrec) {
-                        const int64_t sl = (r0 + u == 0) ? slot0 : 2 * (c_first + r0 + u);
+                        const int64_t sl = (r0 + u == 0) ? slot0 : 2 * (c_first + r0 + u) * NG + gq;
                         lse[u] = __ldcg(reinterpret_cast<const float2*>(p.rec_lse) + (sl * 8 + mt) * 4 + tig);
                         rv[u] = __ldcg(reinterpret_cast<const float4*>(p.rec_o) + (sl * 8 + mt) * 32 + lane);
                     }
@@ -957,14 +1040,15 @@ int env_int(const char* name, int dflt) {
 }
 
 /* Sweep knobs (unset in normal use): PGQA_WARPS, PGQA_STAGES, PGQA_MIN_CHUNKS, PGQA_GRID,
- * PGQA_NO_PDL (plain launch instead of a programmatic dependent launch). */
+ * PGQA_NO_PDL (plain launch instead of a programmatic dependent launch), PGQA_NG (1: one
+ * row group per unit even where two would share the K/V tiles). */
 struct Knobs {
-    int warps, stages, min_chunks, grid, no_pdl;
+    int warps, stages, min_chunks, grid, no_pdl, ng;
 };
 const Knobs& knobs() {
     static const Knobs k = {env_int("PGQA_WARPS", 0), env_int("PGQA_STAGES", 0),
                             env_int("PGQA_MIN_CHUNKS", 0), env_int("PGQA_GRID", 0),
-                            env_int("PGQA_NO_PDL", 0)};
+                            env_int("PGQA_NO_PDL", 0), env_int("PGQA_NG", 0)};
     return k;
 }
 
@@ -977,15 +1061,19 @@ constexpr int kB200SmemOptin = 232448;
 
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
-int smem_bytes_for(int warps, int stages, int64_t B, bool kv8) {
+int smem_bytes_for(int warps, int stages, int64_t B, bool kv8, int ng) {
     size_t s = 1024;  // alignment slack for the 1024-byte aligned ring
     s += (size_t)warps * stages * (kv8 ? kStageBytesKv8 : kStageBytes);
     s += (size_t)warps * stages * 8;
-    s += (size_t)(32 + 4 * warps) * 4;           // warp sums + parked keys
+    s += (size_t)(32 + 4 * warps * ng) * 4;      // warp sums + parked keys
     s += align_up((size_t)(B + 1) * 4, 16) + 16;  // prefix table (+ alignment of what follows)
-    if (kv8) s += (size_t)warps * sizeof(Stash);  // early stash slots
+    if (kv8 || ng > 1) s += (size_t)warps * ng * sizeof(Stash);  // early stash slots
     return (int)s;
 }
+
+/* Row groups per unit: 2 where a KV head has more than one group of 8 query rows and
+ * the (warps, stages) pair has a two-group instantiation. */
+bool ng2_compiled(int w, int s, bool kv8) { return w == 8 && s == (kv8 ? 4 : 2); }
 
 /* Instantiated (warps, stages) pairs.  A warp's two parked states reuse its own ring,
  * so every pair must give a ring of at least 2 * sizeof(Stash) per warp. */
@@ -1004,18 +1092,23 @@ int validate_shape(int64_t B, int64_t Hq, int64_t Hkv, int64_t D, int64_t P) {
 }
 
 /* Workspace layout: [error word | record lse | record o | arrival counters].  The record
- * regions depend only on the grid, so the counters start at the same offset for every
- * shape: a workspace reused across shapes never reads old records as counters. */
-size_t record_lse_bytes(int grid) { return align_up((size_t)2 * grid * 8 * 8 * 4, 256); }
-
-size_t records_bytes(int grid) {
-    return record_lse_bytes(grid) + align_up((size_t)2 * grid * 8 * kHeadDim * 4, 256);
+ * regions depend only on the grid (sized for the largest row-group count per unit), so
+ * the counters start at the same offset for every shape: a workspace reused across
+ * shapes never reads old records as counters. */
+constexpr int kMaxGroupsPerUnit = 2;
+size_t record_lse_bytes(int grid) {
+    return align_up((size_t)2 * grid * kMaxGroupsPerUnit * 8 * 8 * 4, 256);
 }
 
-int64_t workspace_bytes_for(int64_t B, int64_t U, int grid) {
+size_t records_bytes(int grid) {
+    return record_lse_bytes(grid) +
+           align_up((size_t)2 * grid * kMaxGroupsPerUnit * 8 * kHeadDim * 4, 256);
+}
+
+int64_t workspace_bytes_for(int64_t B, int64_t U, int ng, int grid) {
     size_t s = 256;                                   // error word (+ pad)
     s += records_bytes(grid);                         // record lse + record o
-    s += align_up((size_t)B * U * 8 * 4, 256);        // arrival counters per M tile
+    s += align_up((size_t)B * U * ng * 8 * 4, 256);   // arrival counters per row group, M tile
     return (int64_t)s;
 }
 
@@ -1039,9 +1132,12 @@ int make_plan_impl(int64_t B, int64_t Sq, int64_t Hq, int64_t Hkv, int64_t D, in
         w = kDefaultWarps;
         s = kv8 ? kDefaultStagesKv8 : kDefaultStages;
     }
+    // Two row groups per unit when they exist and that instantiation fits as it is.
+    int ng = (n_hg >= 2 && kn.ng != 1 && ng2_compiled(w, s, kv8) &&
+              smem_bytes_for(w, s, B, kv8, 2) <= smem_optin) ? 2 : 1;
     // Deepest ring that fits next to the per-sequence prefix table.
-    while (smem_bytes_for(w, s, B, kv8) > smem_optin && variant_compiled(w, s - 1, kv8)) --s;
-    if (smem_bytes_for(w, s, B, kv8) > smem_optin) {
+    while (smem_bytes_for(w, s, B, kv8, ng) > smem_optin && variant_compiled(w, s - 1, kv8)) --s;
+    if (smem_bytes_for(w, s, B, kv8, ng) > smem_optin) {
         plan->status = PGQA_ERR_UNSUPPORTED;  // batch too large for the in-CTA prefix table
         return plan->status;
     }
@@ -1049,10 +1145,12 @@ int make_plan_impl(int64_t B, int64_t Sq, int64_t Hq, int64_t Hkv, int64_t D, in
     plan->stages = s;
     plan->grid_ctas = kn.grid > 0 ? kn.grid : sms;
     plan->min_chunks_per_warp = kn.min_chunks > 0 ? kn.min_chunks : kDefaultMinChunks;
+    const int64_t n_w = ceil_div64(n_hg, ng);
     plan->head_groups = (int32_t)n_hg;
-    plan->units_per_seq = (int32_t)(Hkv * n_hg);
-    plan->smem_bytes = smem_bytes_for(w, s, B, kv8);
-    plan->workspace_bytes = workspace_bytes_for(B, Hkv * n_hg, plan->grid_ctas);
+    plan->groups_per_unit = ng;
+    plan->units_per_seq = (int32_t)(Hkv * n_w);
+    plan->smem_bytes = smem_bytes_for(w, s, B, kv8, ng);
+    plan->workspace_bytes = workspace_bytes_for(B, Hkv * n_w, ng, plan->grid_ctas);
     plan->status = PGQA_OK;
     return PGQA_OK;
 }
@@ -1168,10 +1266,10 @@ int lib_workspace(int dev, size_t need, void** out) {
     return PGQA_OK;
 }
 
-template <int W, int S, bool MQ, bool KV8>
+template <int W, int S, bool MQ, bool KV8, int NG>
 int launch_variant(const CUtensorMap& km, const CUtensorMap& vm, const DecodeParams& p, int grid,
                    int smem, cudaStream_t stream) {
-    auto kern = pgqa_decode_kernel<W, S, MQ, KV8>;
+    auto kern = pgqa_decode_kernel<W, S, MQ, KV8, NG>;
     static int configured_smem[kMaxDevices] = {0};  // one table per instantiation
     int dev = 0;
     cudaGetDevice(&dev);
@@ -1206,19 +1304,24 @@ int launch_t(const pgqa_plan& plan, const CUtensorMap& km, const CUtensorMap& vm
              const DecodeParams& p, cudaStream_t stream) {
     const int w = plan.warps_per_cta, s = plan.stages;
     const int g = plan.grid_ctas, sm = plan.smem_bytes;
-    if (KV8) {
-        if (w == 12 && s == 3) return launch_variant<12, 3, MQ, true>(km, vm, p, g, sm, stream);
-        if (w == 8 && s == 4) return launch_variant<8, 4, MQ, true>(km, vm, p, g, sm, stream);
-        if (w == 8 && s == 3) return launch_variant<8, 3, MQ, true>(km, vm, p, g, sm, stream);
-        if (w == 8 && s == 6) return launch_variant<8, 6, MQ, true>(km, vm, p, g, sm, stream);
+    if (plan.groups_per_unit == 2) {
+        if (KV8 && w == 8 && s == 4) return launch_variant<8, 4, MQ, true, 2>(km, vm, p, g, sm, stream);
+        if (!KV8 && w == 8 && s == 2) return launch_variant<8, 2, MQ, false, 2>(km, vm, p, g, sm, stream);
         return PGQA_ERR_UNSUPPORTED;
     }
-    if (w == 4 && s == 6) return launch_variant<4, 6, MQ, false>(km, vm, p, g, sm, stream);
-    if (w == 4 && s == 5) return launch_variant<4, 5, MQ, false>(km, vm, p, g, sm, stream);
-    if (w == 4 && s == 4) return launch_variant<4, 4, MQ, false>(km, vm, p, g, sm, stream);
-    if (w == 4 && s == 3) return launch_variant<4, 3, MQ, false>(km, vm, p, g, sm, stream);
-    if (w == 8 && s == 3) return launch_variant<8, 3, MQ, false>(km, vm, p, g, sm, stream);
-    if (w == 8 && s == 2) return launch_variant<8, 2, MQ, false>(km, vm, p, g, sm, stream);
+    if (KV8) {
+        if (w == 12 && s == 3) return launch_variant<12, 3, MQ, true, 1>(km, vm, p, g, sm, stream);
+        if (w == 8 && s == 4) return launch_variant<8, 4, MQ, true, 1>(km, vm, p, g, sm, stream);
+        if (w == 8 && s == 3) return launch_variant<8, 3, MQ, true, 1>(km, vm, p, g, sm, stream);
+        if (w == 8 && s == 6) return launch_variant<8, 6, MQ, true, 1>(km, vm, p, g, sm, stream);
+        return PGQA_ERR_UNSUPPORTED;
+    }
+    if (w == 4 && s == 6) return launch_variant<4, 6, MQ, false, 1>(km, vm, p, g, sm, stream);
+    if (w == 4 && s == 5) return launch_variant<4, 5, MQ, false, 1>(km, vm, p, g, sm, stream);
+    if (w == 4 && s == 4) return launch_variant<4, 4, MQ, false, 1>(km, vm, p, g, sm, stream);
+    if (w == 4 && s == 3) return launch_variant<4, 3, MQ, false, 1>(km, vm, p, g, sm, stream);
+    if (w == 8 && s == 3) return launch_variant<8, 3, MQ, false, 1>(km, vm, p, g, sm, stream);
+    if (w == 8 && s == 2) return launch_variant<8, 2, MQ, false, 1>(km, vm, p, g, sm, stream);
     return PGQA_ERR_UNSUPPORTED;
 }
 
@@ -1304,6 +1407,7 @@ int decode_impl(const void* q, const void* k, const void* v, void* out, const in
     p.Hkv = (int32_t)Hkv;
     p.g = (int32_t)g;
     p.n_hg = plan.head_groups;
+    p.n_w = plan.units_per_seq / (int32_t)Hkv;
     p.U = plan.units_per_seq;
     p.Sq = (int32_t)Sq;
     p.rows = (int32_t)(g * Sq);

@@ -137,3 +137,18 @@ def test_workspace_size_is_zero_for_invalid_shapes():
     assert L.pgqa_last_status() == 3
     # more query tokens -> more row groups per KV head -> more arrival counters
     assert L.pgqa_workspace_size_v2(4, 4, 32, 8, 128, 16) > L.pgqa_workspace_size(4, 32, 8, 128, 16)
+
+
+def test_plan_carries_two_row_groups_per_unit_when_a_kv_head_has_more():
+    """g = 16: two groups of 8 query rows per KV head share every K/V tile (one unit per
+    KV head instead of two); g <= 8 keeps one group per unit."""
+    L = _lib.lib()
+    wide = _lib.PgqaPlan()
+    assert L.pgqa_make_plan(4, 64, 4, 128, 16, 148, 232448, ctypes.byref(wide)) == 0
+    assert (wide.head_groups, wide.groups_per_unit, wide.units_per_seq) == (2, 2, 4)
+    odd = _lib.PgqaPlan()  # 3 groups -> 2 units per KV head, the last one half empty
+    assert L.pgqa_make_plan(4, 48, 2, 128, 16, 148, 232448, ctypes.byref(odd)) == 0
+    assert (odd.head_groups, odd.groups_per_unit, odd.units_per_seq) == (3, 2, 4)
+    narrow = _lib.PgqaPlan()
+    assert L.pgqa_make_plan(4, 32, 8, 128, 16, 148, 232448, ctypes.byref(narrow)) == 0
+    assert (narrow.head_groups, narrow.groups_per_unit, narrow.units_per_seq) == (1, 1, 8)
