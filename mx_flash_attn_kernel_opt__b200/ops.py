@@ -98,6 +98,13 @@ def decode(q, k_cache, v_cache, block_table, seq_lens, scale=None, out=None,
     if out is None:
         out = torch.empty_like(q)
     _check_tensors(q, k_cache, v_cache, out, seq_lens, block_table)
+    if tuple(out.shape) != tuple(q.shape):
+        raise PgqaError(2, f"decode: out {tuple(out.shape)} must have q's shape {tuple(q.shape)}")
+    if q.dim() not in (3, 4):
+        raise PgqaError(2, "decode: q must be [B, Hq, D] or [B, Sq, Hq, D]")
+    devs = {t.device for t in (q, k_cache, v_cache, out, seq_lens, block_table)}
+    if len(devs) != 1:
+        raise ValueError(f"decode: all tensors must be on one device, got {sorted(map(str, devs))}")
     B = q.shape[0]
     Hq, D = q.shape[-2], q.shape[-1]
     Sq = q.shape[1] if q.dim() == 4 else 1

@@ -292,3 +292,16 @@ def test_batch_beyond_prefix_table_is_refused(cuda_device):
     with pytest.raises(pgqa.PgqaError) as e:
         pgqa.decode(inp.q, inp.k, inp.v, inp.block_table, inp.seq_lens)
     assert e.value.status == 3
+
+
+def test_python_surface_rejects_mismatched_output(cuda_device):
+    """The operator refuses an output whose shape differs from q's (it would write past
+    it) before anything is launched."""
+    inp = inputs.baseline_config("c1").to(cuda_device)
+    q4 = inp.q.unsqueeze(1).expand(-1, 2, -1, -1).contiguous()  # two query tokens
+    small = torch.zeros_like(inp.q)                                 # one token's worth
+    with pytest.raises(pgqa.PgqaError) as e:
+        pgqa.decode(q4, inp.k, inp.v, inp.block_table, inp.seq_lens, out=small)
+    assert e.value.status == 2
+    with pytest.raises(ValueError):
+        pgqa.decode(inp.q, inp.k, inp.v, inp.block_table, inp.seq_lens.cpu())
