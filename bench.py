@@ -21,6 +21,9 @@ cpu_baseline  the CPU oracle (fp32 PyTorch paged attention, all host threads) on
 
 scaling_reference  (N=1 lines) c5, the workload the N>1 runs shard, on this one GPU.
 
+--seqlen-q S decodes S query tokens per sequence with the end-aligned causal mask
+(speculative / multi-token decode, an extension): value still counts the KV bytes once.
+
 --kv fp8 runs the same workload with e4m3 KV pages (per-KV-head scales; an extension,
 the reference's pools are bf16): value counts the e4m3 bytes; no e2e or CPU leg.
 
@@ -61,6 +64,9 @@ def parse():
     ap.add_argument("--out", default=None, help="also append the JSON line to this file")
     ap.add_argument("--profile", type=int, default=0,
                     help="run N decode calls of the workload and exit (for ncu captures)")
+    ap.add_argument("--seqlen-q", type=int, default=1,
+                    help="query tokens per sequence (causal, end-aligned; >1 is speculative / "
+                         "multi-token decode, an extension of the reference)")
     ap.add_argument("--kv", default="bf16", choices=["bf16", "fp8"],
                     help="KV page format: bf16 (the reference's) or e4m3 with per-head scales")
     return ap.parse_args()
@@ -276,6 +282,11 @@ def main():
     if fp8:
         inp = inputs.to_fp8(inp, keep_device=True)
         torch.cuda.empty_cache()
+    Sq = max(1, args.seqlen_q)
+    if Sq > 1:  # Sq query tokens per sequence, q / out [B, Sq, Hq, D]
+        g_q = torch.Generator(device=dev).manual_seed(1234)
+        qm = torch.randn((inp.batch, Sq, inp.num_heads, 128), generator=g_q, device=dev)
+        inp.q = qm.to(torch.bfloat16)
     kv_bytes = inp.kv_bytes()
     alg_bytes = inp.algorithmic_bytes()
 
@@ -287,24 +298,32 @@ def main():
     for _ in range(copies - 1):
         sets.append((inp.k.clone(), inp.v.clone()))
     out = torch.empty_like(inp.q)
-    ws = ops.workspace_for(inp.batch, inp.num_heads, inp.num_heads_k, 128, inp.page_size, dev)
+    ws = ops.workspace_for(inp.batch, inp.num_heads, inp.num_heads_k, 128, inp.page_size, dev,
+                           seqlen_q=Sq)
     stream = torch.cuda.current_stream(dev)
 
     # one correctness-checked call through the Python wrapper, then prebuilt C calls
     ops.decode(inp.q, inp.k, inp.v, inp.block_table, inp.seq_lens, scale=inp.scale, out=out,
-               workspace=ws, k_scale=inp.k_scale, v_scale=inp.v_scale)
+               workspace=ws, k_scale=inp.k_scale, v_scale=inp.v_scale, causal=Sq > 1)
     L = _lib.lib()
     vp = ctypes.c_void_p
     sh = vp(stream.cuda_stream)
     if fp8:
         argsets = [(vp(inp.q.data_ptr()), vp(k.data_ptr()), vp(v.data_ptr()), None, None,
                     vp(out.data_ptr()), vp(inp.seq_lens.data_ptr()),
-                    vp(inp.block_table.data_ptr()), inp.batch, 1, 0, inp.num_heads,
+                    vp(inp.block_table.data_ptr()), inp.batch, Sq, 0, inp.num_heads,
                     inp.num_heads_k, 128, inp.page_size, inp.num_pages,
-                    inp.block_table.stride(0), 0, 0, ctypes.c_float(inp.scale),
+                    inp.block_table.stride(0), 0, int(Sq > 1), ctypes.c_float(inp.scale),
                     vp(inp.k_scale.data_ptr()), vp(inp.v_scale.data_ptr()), vp(ws.data_ptr()),
                     ws.numel(), sh) for (k, v) in sets]
         fn, fn_name = L.pgqa_decode_fp8, "pgqa_decode_fp8"
+    elif Sq > 1:
+        argsets = [(vp(inp.q.data_ptr()), vp(k.data_ptr()), vp(v.data_ptr()), vp(out.data_ptr()),
+                    vp(inp.seq_lens.data_ptr()), vp(inp.block_table.data_ptr()), inp.batch, Sq,
+                    inp.num_heads, inp.num_heads_k, 128, inp.page_size, inp.num_pages,
+                    inp.block_table.stride(0), 0, 1, ctypes.c_float(inp.scale), vp(ws.data_ptr()),
+                    ws.numel(), sh) for (k, v) in sets]
+        fn, fn_name = L.pgqa_decode_v2, "pgqa_decode_v2"
     else:
         argsets = [(vp(inp.q.data_ptr()), vp(k.data_ptr()), vp(v.data_ptr()), vp(out.data_ptr()),
                     vp(inp.seq_lens.data_ptr()), vp(inp.block_table.data_ptr()), inp.batch,
@@ -416,7 +435,7 @@ def main():
 
     # ---- end to end through the C symbol with host buffers ----
     e2e = None
-    if not args.no_e2e and not fp8:
+    if not args.no_e2e and not fp8 and Sq == 1:
         e2e = e2e_measure(inp, dev, stream, steps, args.e2e_host_budget_gb, world)
         if world > 1:
             t = torch.tensor([e2e.pop("_ms"), e2e.pop("_kv")], dtype=torch.float64, device=dev)
@@ -430,11 +449,11 @@ def main():
             e2e["value"] = round(kvb / (ms / 1e3) / 1e9, 3)
 
     scaling_ref = None
-    if world == 1 and not args.no_scaling_ref and not fp8 and name != "c5":
+    if world == 1 and not args.no_scaling_ref and not fp8 and Sq == 1 and name != "c5":
         scaling_ref = scaling_reference(dev, stream)
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline and not fp8:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and not fp8 and Sq == 1:
         cpu = time_cpu_oracle(name, budget_s=10.0)
 
     if rank == 0:
@@ -448,6 +467,7 @@ def main():
             "config": {"workload": describe(name, world),
                        "kv_bytes_per_call": int(kv_total),
                        "kv_format": args.kv,
+                       "seqlen_q": Sq, "causal": Sq > 1,
                        "l2": (f"{len(sets)} rotating K/V pool copies, "
                               f"{len(sets) * kv_bytes / 1e6:.0f} MB read set per rank "
                               f"(> L2 {L2_BYTES / 1e6:.0f} MB)"),

@@ -43,7 +43,7 @@ class DecodeInputs:
 
     @property
     def num_heads(self):
-        return self.q.shape[1]
+        return self.q.shape[-2]  # q is [B, Hq, D] or [B, Sq, Hq, D]
 
     @property
     def num_heads_k(self):
@@ -64,10 +64,10 @@ class DecodeInputs:
 
     def algorithmic_bytes(self):
         """KV bytes + q and out + the block-table entries and lengths actually read."""
-        B, Hq = self.batch, self.num_heads
+        q_elems = self.q.numel()  # [B, (Sq,) Hq, D]: q read and out written once each
         pages = int(((self.seq_lens.to(torch.int64) + self.page_size - 1)
                      // self.page_size).sum().item())
-        return self.kv_bytes() + 2 * B * Hq * HEAD_DIM * 2 + pages * 4 + B * 4
+        return self.kv_bytes() + 2 * q_elems * 2 + pages * 4 + self.batch * 4
 
     def to(self, device):
         mv = (lambda t: None if t is None else t.to(device))
