@@ -168,7 +168,7 @@ int pgqa_append_kv_fp8(const void* k_new, const void* v_new, void* k_cache, void
  * point takes the same arguments as pgqa_decode_v1 minus the workspace and allocates
  * nothing: its scratch (split records and arrival counters) lives in a fixed 4 MiB
  * device array inside the library, which every GPU that loads the library holds until
- * the process exits.  Shapes needing more (about 90,000 sequence x KV-head units on a
+ * the process exits.  Shapes needing more (about 50,000 sequence x KV-head units on a
  * 148-SM B200) are rejected with PGQA_ERR_SCRATCH_LIMIT before anything is launched.
  * The caller still passes q, the pools, seq_lens, block_table and out.
  *

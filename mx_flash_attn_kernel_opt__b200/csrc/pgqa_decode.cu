@@ -1764,8 +1764,8 @@ extern "C" const char* pgqa_version(void) { return "pgqa-b200 0.1 (sm_100a)"; }
 /* Scratch for pgqa_decode_noalloc: the same layout pgqa_decode_v1 expects of a caller's
  * workspace (error word, split records, arrival counters), held in a fixed array that
  * every GPU loading this library keeps until the process exits.  4 MiB covers the
- * records of a 148-SM B200 plus arrival counters for about 90,000 (sequence, KV head,
- * head group) units. */
+ * records of a 148-SM B200 (2.6 MB, sized for two row groups per unit) plus arrival
+ * counters for about 50,000 (sequence, KV head, row group) units. */
 constexpr size_t kNoAllocScratchBytes = (size_t)4 << 20;
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
 
