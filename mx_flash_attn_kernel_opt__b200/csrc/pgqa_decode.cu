@@ -975,10 +975,11 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
             __syncwarp();  // the warp's record stores happen before lane 0's release
             if (lane == 0) {
                 int32_t* cnt = p.counters + (((int64_t)ub * p.U + uu) * NG + gq) * 8 + mt;
-                ptx::fence_acq_rel_gpu();  // release this CTA's record tile
-                const int32_t prev = ptx::atom_add_relaxed_gpu(cnt, 1);
+                // releases this CTA's record tile (the warp's stores, ordered before lane 0
+                // by the __syncwarp above) and, for the last arriver, acquires the others'
+                // (one acq_rel atomic measured faster than fence + relaxed atomic + fence)
+                const int32_t prev = ptx::atom_add_acq_rel_gpu(cnt, 1);
                 if (prev == (int32_t)(c_last - c_first)) {
-                    ptx::fence_acq_rel_gpu();  // acquire the other CTAs' tiles
                     *cnt = 0;                  // leave the workspace zeroed for the next call
                     last = 1;
                 }

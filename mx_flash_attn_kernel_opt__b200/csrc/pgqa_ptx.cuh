@@ -72,15 +72,13 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-/* GPU-scope acquire-release fence (lighter than the sequentially consistent
- * fence __threadfence emits); pairs with relaxed atomics on arrival counters. */
-__device__ __forceinline__ void fence_acq_rel_gpu() {
-    asm volatile("fence.acq_rel.gpu;" ::: "memory");
-}
-
-__device__ __forceinline__ int32_t atom_add_relaxed_gpu(int32_t* ptr, int32_t v) {
+/* Atomic add with acquire-release semantics at GPU scope: the issuing thread's earlier
+ * writes -- and, release being cumulative, the writes of lanes ordered before it by a
+ * warp barrier -- are visible before the add; loads after it see what other threads
+ * released before their own add. */
+__device__ __forceinline__ int32_t atom_add_acq_rel_gpu(int32_t* ptr, int32_t v) {
     int32_t old;
-    asm volatile("atom.add.relaxed.gpu.global.s32 %0, [%1], %2;"
+    asm volatile("atom.add.acq_rel.gpu.global.s32 %0, [%1], %2;"
                  : "=r"(old)
                  : "l"(ptr), "r"(v)
                  : "memory");
