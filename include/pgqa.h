@@ -56,7 +56,9 @@ enum pgqa_status {
  * Errors (which the reference ignores) are recorded and can be read back with
  * pgqa_last_status().  The first call on a device allocates the library's
  * per-device workspace (cudaMalloc), so the first call must not be inside a
- * CUDA-graph capture.
+ * CUDA-graph capture.  Like the reference's static buffers, that workspace is shared
+ * by every run_kernel call on the device: calls that may overlap on the GPU (several
+ * streams or host threads) must use pgqa_decode_v1/_v2 with a workspace each.
  * Beyond the reference (which fixes seqlen_q = 1, causal = 0; task.md:64-66),
  * seqlen_q >= 1 query tokens per sequence are accepted, q and output being
  * (B, seqlen_q, Hq, D); with causal = 1 token i sees keys [0, L - seqlen_q + i].
