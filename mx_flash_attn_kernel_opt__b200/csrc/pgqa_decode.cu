@@ -21,15 +21,15 @@
  *     from a 32-entry block-table window loaded by the whole warp; only the first
  *     ceil(L_b / page_size) entries of a row are ever read.
  *   * Math per 16-token stage, tokens in the MMA M dimension ("swap AB"), 8 query rows
- *     of one KV head in N (a head group; with seqlen_q tokens a row is a (head, token)
- *     pair):  S^T = K.Q^T (8 x mma.m16n8k16 bf16), fp32 online softmax in the log2
+ *     of one KV head in N (a row group; with seqlen_q tokens a row is a (head, token)
+ *     pair; with several row groups per KV head a warp carries two over each tile):  S^T = K.Q^T (8 x mma.m16n8k16 bf16), fp32 online softmax in the log2
  *     domain (scale*log2e folded into one multiply, ex2.approx, a reference max that
  *     moves only when a score exceeds it by 2^8), P^T moved into the B-operand layout
  *     with movmatrix.trans, O^T += V^T.P^T (8 x mma).
  *   * e4m3 pools (KV8): 4 KB stages, one 128-byte box each for K and V; the bytes are
  *     converted exactly to f16 after ldmatrix and multiplied with f16 MMAs, two chunks
  *     per step.
- *   * A unit (b, kv, head-group) that lies inside one warp's slice is normalised and
+ *   * A unit (b, kv, row groups) that lies inside one warp's slice is normalised and
  *     stored as bf16 directly.  Units cut by warp boundaries are merged in shared
  *     memory at the end of the CTA; units cut by CTA boundaries write an fp32 record
  *     (o, log2-sum-exp) to the workspace, and the last CTA to finish the unit (atomic

@@ -9,7 +9,7 @@
  * length exit early (:93).  Here the work is instead measured in 16-token chunks
  * of the *actual* lengths and cut into equal contiguous slices:
  *
- *   unit u = (b, j), j in [0, units_per_seq) = (kv_head, head_group), b-major;
+ *   unit u = (b, j), j in [0, units_per_seq) = (kv_head, group of row groups), b-major;
  *   unit (b, j) owns n_b = ceil(L_b / 16) chunks;
  *   flat chunk index of chunk c of unit (b, j) = pre[b] * U + j * n_b + c,
  *   where pre[b] = sum_{b' < b} n_b' and U = units_per_seq;
@@ -35,7 +35,7 @@ namespace pgqa {
 
 constexpr int kChunkTokens = 16;   // tokens per pipeline stage / MMA M tile
 constexpr int kHeadDim = 128;      // the only head dimension compiled
-constexpr int kHeadsPerGroup = 8;  // query heads per MMA N tile
+constexpr int kHeadsPerGroup = 8;  // query rows per MMA N tile (a row group)
 
 PGQA_HD int64_t ceil_div64(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
