@@ -93,6 +93,8 @@ struct DecodeParams {
     int64_t cap_tokens;  // bt_stride * page_size (clamp for seq_lens)
     float scale_log2;    // scale * log2(e)
     int32_t min_chunks;
+    int32_t spec_chunks;     // chunks per warp prefetched into L2 before griddepcontrol.wait
+    int32_t debug_spec_skew; // test hook: added to every length the speculative pass reads
     int32_t debug_stuck;     // test hook: CTA 0 / warp 0 first stage expects 16 bytes too many
     uint64_t wait_limit_ns;  // bound on every mbarrier wait
 };
@@ -293,24 +295,16 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
         for (int i = 0; i < W * S; ++i) ptx::mbar_init(ptx::smem_u32(bars + i), 1);
         ptx::fence_mbar_init();
     }
-    // Launched as a programmatic dependent: everything above overlaps the previous
-    // kernel's tail; no global memory is touched before the previous grid is complete.
-    ptx::griddep_wait();
 
-    /* ---- chunk prefix over sequences (every CTA computes it; B is small) ---- */
-    {
-        const int per = (p.B + NT - 1) / NT;
-        const int b0 = min(p.B, tid * per);
-        const int b1 = min(p.B, b0 + per);
+    /* ---- chunk prefix over sequences: pre[b] = chunks before sequence b, pre[B] = all ----
+     * (every CTA computes it; B is small).  Thread tid owns sequences [sb0, sb1). */
+    const int per_thread = (p.B + NT - 1) / NT;
+    const int sb0 = min(p.B, tid * per_thread);
+    const int sb1 = min(p.B, sb0 + per_thread);
+    auto scan_prefix = [&](auto load_len) {
         uint32_t local = 0;
-        int32_t bad = 0;
-        for (int b = b0; b < b1; ++b) {
-            const int32_t L0 = __ldg(p.seq_lens + b);
-            const int64_t L = (int64_t)L0 + p.len_add;
-            if (L0 < 0 || L > p.cap_tokens) bad = 1;
-            local += (uint32_t)seq_chunks(L, p.cap_tokens);
-        }
-        if (bad && blockIdx.x == 0) atomicOr(p.err, kErrBadSeqlen);
+        for (int b = sb0; b < sb1; ++b)
+            local += (uint32_t)seq_chunks((int64_t)load_len(b) + p.len_add, p.cap_tokens);
         uint32_t incl = local;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
@@ -319,15 +313,95 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
         }
         if (lane == 31) misc[warp] = (int32_t)incl;
         __syncthreads();
-        uint32_t base = 0;
-        for (int w2 = 0; w2 < warp; ++w2) base += (uint32_t)misc[w2];
-        uint32_t run = base + incl - local;
-        for (int b = b0; b < b1; ++b) {
+        uint32_t run = incl - local;
+        for (int w2 = 0; w2 < warp; ++w2) run += (uint32_t)misc[w2];
+        if (tid == NT - 1) pre[p.B] = run + local;
+        for (int b = sb0; b < sb1; ++b) {
             pre[b] = run;
-            run += (uint32_t)seq_chunks(keys_of(p, b), p.cap_tokens);
+            run += (uint32_t)seq_chunks((int64_t)load_len(b) + p.len_add, p.cap_tokens);
         }
-        if (tid == NT - 1) pre[p.B] = base + incl;
         __syncthreads();
+    };
+
+    /* ---- speculative pass, while the previous grid finishes on other SMs ----
+     * The prefix table and the partition are computed from a first read of the lengths
+     * and the block table, and each warp prefetches its first chunks into L2.  Only L2
+     * sees these reads (ld.global.cg and tensor prefetches; L2 is coherent with the
+     * previous grid's writes).  After griddepcontrol.wait every length is read again and
+     * the table is kept only if every sequence still has the chunk count it was built
+     * from (else it is rebuilt); the block table is read again too, so a predecessor
+     * that writes lengths or table only makes the prefetch miss.  Table entries are read
+     * only below ceil(L/P) of the clamped length (inside every row by the table's
+     * contract) and page ids outside [0, num_pages) are not prefetched. */
+    if (p.spec_chunks > 0) {
+        scan_prefix([&](int b) { return ptx::ld_cg_s32(p.seq_lens + b) + p.debug_spec_skew; });
+        const int64_t T = (int64_t)pre[p.B] * p.U;
+        const int64_t nct = T > 0 ? active_ctas(T, gridDim.x, W, p.min_chunks) : 0;
+        if ((int64_t)blockIdx.x < nct) {
+            const int64_t cs = slice_begin(blockIdx.x, nct, T);
+            const int64_t clen = slice_begin(blockIdx.x + 1, nct, T) - cs;
+            const int wa = (int)active_warps(clen, W);
+            if (warp < wa) {
+                const int64_t ws = cs + slice_begin(warp, wa, clen);
+                const int64_t ntot = cs + slice_begin(warp + 1, wa, clen) - ws;
+                const int64_t npf = ntot < p.spec_chunks ? ntot : p.spec_chunks;
+                const int P = p.page_size;
+                int32_t b = find_seq(pre, p.B, p.U, ws);
+                int32_t n = (int32_t)(pre[b + 1] - pre[b]);
+                const int64_t r = ws - (int64_t)pre[b] * p.U;
+                int32_t j = (int32_t)(r / n);
+                int32_t c = (int32_t)(r - (int64_t)j * n);
+                int32_t win_b = -1, win_p0 = 0, win_pid = 0;
+                for (int64_t k = 0; k < npf; ++k) {
+                    const int32_t page = (c * kChunkTokens) / P;
+                    if (b != win_b || page < win_p0 || page >= win_p0 + 32) {
+                        win_b = b;
+                        win_p0 = page;
+                        const int32_t npg = (n * kChunkTokens + P - 1) / P;
+                        const int32_t pg = page + lane;
+                        win_pid = (pg < npg)
+                                      ? ptx::ld_cg_s32(p.block_table + (int64_t)b * p.bt_stride + pg)
+                                      : -1;
+                    }
+                    const int32_t pid = __shfl_sync(0xffffffffu, win_pid, page - win_p0);
+                    if (lane == 0 && (uint32_t)pid < (uint32_t)p.num_pages) {
+                        const int32_t kvh = j / p.n_w;
+                        const int32_t z = pid * P + (c * kChunkTokens - page * P);
+                        ptx::tma_prefetch_l2_3d(&kmap, 0, kvh, z);
+                        ptx::tma_prefetch_l2_3d(&vmap, 0, kvh, z);
+                        if (!KV8) {
+                            ptx::tma_prefetch_l2_3d(&kmap, 64, kvh, z);
+                            ptx::tma_prefetch_l2_3d(&vmap, 64, kvh, z);
+                        }
+                    }
+                    if (k + 1 < npf && ++c == n) {  // step to the next chunk (one exists)
+                        c = 0;
+                        if (++j == p.U) {
+                            j = 0;
+                            do { ++b; } while (pre[b + 1] == pre[b]);
+                            n = (int32_t)(pre[b + 1] - pre[b]);
+                        }
+                    }
+                }
+            }
+        }
+    }
+
+    // Launched as a programmatic dependent: everything above overlaps the previous
+    // kernel's tail; of what was read before this point only the checked prefix table
+    // is used after it.
+    ptx::griddep_wait();
+
+    {
+        int32_t bad = 0, changed = p.spec_chunks <= 0;
+        for (int b = sb0; b < sb1; ++b) {
+            const int32_t L0 = __ldg(p.seq_lens + b);
+            const int64_t L = (int64_t)L0 + p.len_add;
+            if (L0 < 0 || L > p.cap_tokens) bad = 1;
+            if ((uint32_t)seq_chunks(L, p.cap_tokens) != pre[b + 1] - pre[b]) changed = 1;
+        }
+        if (bad && blockIdx.x == 0) atomicOr(p.err, kErrBadSeqlen);
+        if (__syncthreads_or(changed)) scan_prefix([&](int b) { return __ldg(p.seq_lens + b); });
     }
 
     /* Zero-length sequences produce zeros (softmax over an empty set), written by CTA 0. */
@@ -843,7 +917,7 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
     }
 
     // Streaming is over: let the next kernel in the stream start launching (it still
-    // waits for this grid's completion before it reads any memory).
+    // waits for this grid's completion before it uses any memory it reads).
     ptx::griddep_launch_dependents();
 
     /* ---- park this warp's cut units in its own (now idle) ring: no TMA is in flight ----
@@ -1042,16 +1116,22 @@ int env_int(const char* name, int dflt) {
 
 /* Sweep knobs (unset in normal use): PGQA_WARPS, PGQA_STAGES, PGQA_MIN_CHUNKS, PGQA_GRID,
  * PGQA_NO_PDL (plain launch instead of a programmatic dependent launch), PGQA_NG (1: one
- * row group per unit even where two would share the K/V tiles). */
+ * row group per unit even where two would share the K/V tiles), PGQA_SPEC (chunks per
+ * warp prefetched into L2 before griddepcontrol.wait; 0: none). */
 struct Knobs {
-    int warps, stages, min_chunks, grid, no_pdl, ng;
+    int warps, stages, min_chunks, grid, no_pdl, ng, spec;
 };
 const Knobs& knobs() {
-    static const Knobs k = {env_int("PGQA_WARPS", 0), env_int("PGQA_STAGES", 0),
+    static const Knobs k = {env_int("PGQA_WARPS", 0),      env_int("PGQA_STAGES", 0),
                             env_int("PGQA_MIN_CHUNKS", 0), env_int("PGQA_GRID", 0),
-                            env_int("PGQA_NO_PDL", 0), env_int("PGQA_NG", 0)};
+                            env_int("PGQA_NO_PDL", 0),     env_int("PGQA_NG", 0),
+                            env_int("PGQA_SPEC", -1)};
     return k;
 }
+
+// chunks per warp prefetched into L2 before griddepcontrol.wait (bf16 / e4m3 pools)
+constexpr int kDefaultSpecChunks = 4;
+constexpr int kDefaultSpecChunksKv8 = 4;
 
 constexpr int kDefaultWarps = 8;
 constexpr int kDefaultStages = 2;
@@ -1422,10 +1502,13 @@ int decode_impl(const void* q, const void* k, const void* v, void* out, const in
     p.cap_tokens = cap;
     p.scale_log2 = scale * 1.4426950408889634f;
     p.min_chunks = plan.min_chunks_per_warp;
+    p.spec_chunks = knobs().spec >= 0 ? knobs().spec : kv8 ? kDefaultSpecChunksKv8 : kDefaultSpecChunks;
     // Test hooks, read per call: PGQA_DEBUG_STUCK_BARRIER=1 makes one stage barrier wait
     // for 16 bytes that never arrive (its wait expires -> PGQA_ERR_DEVICE_TIMEOUT);
-    // PGQA_WAIT_LIMIT_NS shortens the bound on every wait.
+    // PGQA_WAIT_LIMIT_NS shortens the bound on every wait; PGQA_DEBUG_SPEC_SKEW=n adds n
+    // to the lengths the speculative pass sees, as if a predecessor had rewritten them.
     p.debug_stuck = env_int("PGQA_DEBUG_STUCK_BARRIER", 0) != 0;
+    p.debug_spec_skew = env_int("PGQA_DEBUG_SPEC_SKEW", 0);
     {
         const char* lim = getenv("PGQA_WAIT_LIMIT_NS");
         p.wait_limit_ns = (lim && *lim) ? strtoull(lim, nullptr, 10) : kWaitLimitNs;

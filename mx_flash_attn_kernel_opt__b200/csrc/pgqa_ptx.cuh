@@ -95,6 +95,23 @@ __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
+/* 32-bit global load cached in L2 only: it leaves no L1 line that a later load of the
+ * same word could hit. */
+__device__ __forceinline__ int32_t ld_cg_s32(const int32_t* ptr) {
+    int32_t v;
+    asm volatile("ld.global.cg.s32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
+    return v;
+}
+
+/* TMA tiled 3-D prefetch of one box into L2 (no shared memory, no completion). */
+__device__ __forceinline__ void tma_prefetch_l2_3d(const CUtensorMap* map, int32_t x, int32_t y,
+                                                   int32_t z) {
+    asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
+                     reinterpret_cast<uint64_t>(map)),
+                 "r"(x), "r"(y), "r"(z)
+                 : "memory");
+}
+
 /* TMA tiled 3-D load (no multicast) into this CTA's shared memory, completion
  * signalled as tx-bytes on `bar`, with an L2 eviction-priority hint. */
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint32_t bar,

@@ -184,6 +184,24 @@ def test_caller_workspace_on_side_stream(cuda_device):
         pgqa.decode(d.q, d.k, d.v, d.block_table, d.seq_lens, workspace=ws[:need // 2])
 
 
+@pytest.mark.parametrize("skew", [16, -16, 1 << 20])
+def test_speculative_prefix_is_rebuilt_when_lengths_change(skew, cuda_device, monkeypatch):
+    """The pass before griddepcontrol.wait builds the prefix table from a first read of
+    the lengths; PGQA_DEBUG_SPEC_SKEW makes that read disagree with the lengths the call
+    really has (as when a predecessor rewrites them), so the table must be rebuilt after
+    the wait and the output must not change."""
+    inp = inputs.custom_case(6, 32, 4, 16, [1, 17, 300, 2048, 33, 4000], seed=41)
+    d = inp.to(cuda_device)
+    ref = paged_decode_ref(inp.q, inp.k, inp.v, inp.block_table, inp.seq_lens)
+    plain = pgqa.decode(d.q, d.k, d.v, d.block_table, d.seq_lens, scale=inp.scale)
+    monkeypatch.setenv("PGQA_DEBUG_SPEC_SKEW", str(skew))
+    ws = _fresh_ws(inp, cuda_device)
+    out = pgqa.decode(d.q, d.k, d.v, d.block_table, d.seq_lens, scale=inp.scale, workspace=ws)
+    pgqa.check_device_error(ws)
+    assert_parity(out, ref, what=f"skew {skew}")
+    assert torch.equal(out, plain)
+
+
 def test_custom_scale(cuda_device):
     inp = inputs.custom_case(3, 16, 2, 16, [7, 70, 700], seed=21)
     d = inp.to(cuda_device)
