@@ -393,15 +393,26 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
     ptx::griddep_wait();
 
     {
-        int32_t bad = 0, changed = p.spec_chunks <= 0;
-        for (int b = sb0; b < sb1; ++b) {
-            const int32_t L0 = __ldg(p.seq_lens + b);
-            const int64_t L = (int64_t)L0 + p.len_add;
-            if (L0 < 0 || L > p.cap_tokens) bad = 1;
-            if ((uint32_t)seq_chunks(L, p.cap_tokens) != pre[b + 1] - pre[b]) changed = 1;
+        int32_t bad = 0;
+        bool rebuild = true;
+        if (p.spec_chunks > 0) {
+            int32_t changed = 0;
+            for (int b = sb0; b < sb1; ++b) {
+                const int32_t L0 = __ldg(p.seq_lens + b);
+                const int64_t L = (int64_t)L0 + p.len_add;
+                if (L0 < 0 || L > p.cap_tokens) bad = 1;
+                if ((uint32_t)seq_chunks(L, p.cap_tokens) != pre[b + 1] - pre[b]) changed = 1;
+            }
+            rebuild = __syncthreads_or(changed) != 0;
+        }
+        if (rebuild) {
+            scan_prefix([&](int b) {
+                const int32_t L0 = __ldg(p.seq_lens + b);
+                if (L0 < 0 || (int64_t)L0 + p.len_add > p.cap_tokens) bad = 1;
+                return L0;
+            });
         }
         if (bad && blockIdx.x == 0) atomicOr(p.err, kErrBadSeqlen);
-        if (__syncthreads_or(changed)) scan_prefix([&](int b) { return __ldg(p.seq_lens + b); });
     }
 
     /* Zero-length sequences produce zeros (softmax over an empty set), written by CTA 0. */
@@ -1132,6 +1143,17 @@ const Knobs& knobs() {
 // chunks per warp prefetched into L2 before griddepcontrol.wait (bf16 / e4m3 pools)
 constexpr int kDefaultSpecChunks = 4;
 constexpr int kDefaultSpecChunksKv8 = 4;
+// The pass before griddepcontrol.wait is run only when a warp streams at least this many
+// chunks at the table's capacity: it hides behind a previous decode grid's tail, but a
+// call with nothing ahead of it pays its ~2 us in full, which only a long stream repays.
+constexpr int64_t kSpecMinChunksPerWarp = 8;
+
+int spec_chunks_for(int64_t B, const pgqa_plan& plan, int64_t cap_tokens, bool kv8) {
+    if (knobs().spec >= 0) return knobs().spec;
+    const int64_t chunks = B * plan.units_per_seq * ((cap_tokens + kChunkTokens - 1) / kChunkTokens);
+    if (chunks < kSpecMinChunksPerWarp * plan.grid_ctas * plan.warps_per_cta) return 0;
+    return kv8 ? kDefaultSpecChunksKv8 : kDefaultSpecChunks;
+}
 
 constexpr int kDefaultWarps = 8;
 constexpr int kDefaultStages = 2;
@@ -1502,13 +1524,15 @@ int decode_impl(const void* q, const void* k, const void* v, void* out, const in
     p.cap_tokens = cap;
     p.scale_log2 = scale * 1.4426950408889634f;
     p.min_chunks = plan.min_chunks_per_warp;
-    p.spec_chunks = knobs().spec >= 0 ? knobs().spec : kv8 ? kDefaultSpecChunksKv8 : kDefaultSpecChunks;
     // Test hooks, read per call: PGQA_DEBUG_STUCK_BARRIER=1 makes one stage barrier wait
     // for 16 bytes that never arrive (its wait expires -> PGQA_ERR_DEVICE_TIMEOUT);
     // PGQA_WAIT_LIMIT_NS shortens the bound on every wait; PGQA_DEBUG_SPEC_SKEW=n adds n
-    // to the lengths the speculative pass sees, as if a predecessor had rewritten them.
+    // to the lengths the speculative pass sees, as if a predecessor had rewritten them
+    // (and runs that pass whatever the size of the call).
     p.debug_stuck = env_int("PGQA_DEBUG_STUCK_BARRIER", 0) != 0;
     p.debug_spec_skew = env_int("PGQA_DEBUG_SPEC_SKEW", 0);
+    p.spec_chunks = spec_chunks_for(B, plan, cap, kv8);
+    if (p.debug_spec_skew != 0 && p.spec_chunks == 0) p.spec_chunks = kDefaultSpecChunks;
     {
         const char* lim = getenv("PGQA_WAIT_LIMIT_NS");
         p.wait_limit_ns = (lim && *lim) ? strtoull(lim, nullptr, 10) : kWaitLimitNs;
