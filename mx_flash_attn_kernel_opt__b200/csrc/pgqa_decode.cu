@@ -1347,6 +1347,9 @@ int lib_workspace(int dev, size_t need, void** out) {
     std::lock_guard<std::mutex> lk(g_ws_mu);
     LibWorkspace& w = g_ws[dev];
     if (w.ptr == nullptr || w.bytes < need) {
+        // Test hook: PGQA_DEBUG_FAIL_WORKSPACE_ALLOC=1 makes this allocation fail (the
+        // environment is read only here, when an allocation is due).
+        if (env_int("PGQA_DEBUG_FAIL_WORKSPACE_ALLOC", 0) != 0) return PGQA_ERR_WORKSPACE;
         if (w.ptr != nullptr) {
             cudaDeviceSynchronize();
             cudaFree(w.ptr);

@@ -9,6 +9,9 @@ Acceptance, per case:
 """
 import math
 import os
+import subprocess
+import sys
+import textwrap
 
 import pytest
 import torch
@@ -19,6 +22,8 @@ from oracle import match_stats, paged_decode_ref
 from tests._golden import CASES, is_edge, load_rows, make_inputs
 
 pytestmark = pytest.mark.gpu
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 ATOL = RTOL = 1e-2
 
@@ -262,6 +267,43 @@ def test_expired_wait_reports_timeout_and_context_survives(cuda_device, monkeypa
     pgqa.check_device_error(ws)
     ref = paged_decode_ref(inp.q, inp.k, inp.v, inp.block_table, inp.seq_lens)
     assert_parity(out, ref, what="after timeout")
+
+
+def test_library_workspace_allocation_failure_is_reported(cuda_device):
+    """The reference symbol runs on a library-owned workspace, allocated on first use.
+    When that allocation fails (forced by PGQA_DEBUG_FAIL_WORKSPACE_ALLOC in a fresh
+    process, where nothing is allocated yet) the call reports PGQA_ERR_WORKSPACE and
+    leaves the output untouched; once the allocation succeeds the next call runs."""
+    code = textwrap.dedent("""
+        import os, sys, torch
+        sys.path.insert(0, %r)
+        import mx_flash_attn_kernel_opt__b200 as pgqa
+        from mx_flash_attn_kernel_opt__b200 import inputs
+        inp = inputs.spj_case(5, table="permuted")
+        d = inp.to("cuda")
+        out = torch.full_like(d.q, 7.0)
+        B, Hq, D = d.q.shape
+        args = (d.q, d.k, d.v, out, d.seq_lens, d.block_table, B, inp.seqlen_k, 1, Hq,
+                inp.num_heads_k, D, inp.page_size, inp.num_pages, 0)
+        try:
+            pgqa.run_kernel_cabi(*args)
+            print("status 0")
+        except pgqa.PgqaError as e:
+            print("status", e.status)
+        torch.cuda.synchronize()
+        print("untouched", bool((out == 7.0).all()))
+        del os.environ["PGQA_DEBUG_FAIL_WORKSPACE_ALLOC"]
+        pgqa.run_kernel_cabi(*args)
+        torch.cuda.synchronize()
+        pgqa.check_device_error()
+        print("ran", bool(torch.isfinite(out.float()).all()) and bool((out != 7.0).any()))
+    """ % REPO)
+    env = dict(os.environ, PGQA_DEBUG_FAIL_WORKSPACE_ALLOC="1")  # same visible devices
+    r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True,
+                       timeout=600)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = r.stdout.split("\n")
+    assert "status 5" in lines and "untouched True" in lines and "ran True" in lines, r.stdout
 
 
 def test_undersized_or_misaligned_workspace_is_refused(cuda_device):
