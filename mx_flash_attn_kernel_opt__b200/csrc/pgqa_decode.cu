@@ -324,6 +324,8 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
     };
 
     /* ---- speculative pass, while the previous grid finishes on other SMs ----
+     * (Run only when spec_chunks > 0: the host enables it for calls whose warps stream
+     * enough chunks to repay it when no grid is ahead.)
      * The prefix table and the partition are computed from a first read of the lengths
      * and the block table, and each warp prefetches its first chunks into L2.  Only L2
      * sees these reads (ld.global.cg and tensor prefetches; L2 is coherent with the
