@@ -22,10 +22,11 @@
  *     ceil(L_b / page_size) entries of a row are ever read.
  *   * Math per 16-token stage, tokens in the MMA M dimension ("swap AB"), 8 query rows
  *     of one KV head in N (a row group; with seqlen_q tokens a row is a (head, token)
- *     pair; with several row groups per KV head a warp carries two over each tile):  S^T = K.Q^T (8 x mma.m16n8k16 bf16), fp32 online softmax in the log2
- *     domain (scale*log2e folded into one multiply, ex2.approx, a reference max that
- *     moves only when a score exceeds it by 2^8), P^T moved into the B-operand layout
- *     with movmatrix.trans, O^T += V^T.P^T (8 x mma).
+ *     pair; with several row groups per KV head a warp carries two over each tile):
+ *     S^T = K.Q^T (8 x mma.m16n8k16 bf16), fp32 online softmax in the log2 domain
+ *     (scale*log2e folded into one multiply, ex2.approx, a reference max that moves
+ *     only when a score exceeds it by 2^8), P^T moved into the B-operand layout with
+ *     movmatrix.trans, O^T += V^T.P^T (8 x mma).
  *   * e4m3 pools (KV8): 4 KB stages, one 128-byte box each for K and V; the bytes are
  *     converted exactly to f16 after ldmatrix and multiplied with f16 MMAs, two chunks
  *     per step.
@@ -35,7 +36,11 @@
  *     (o, log2-sum-exp) to the workspace, and the last CTA to finish the unit (atomic
  *     counter, reset by that CTA) merges the records -- the LSE combine, fused.
  *   * Launched as a programmatic dependent (griddepcontrol): the prologue overlaps the
- *     previous kernel's tail; no global memory is read before that kernel completes.
+ *     previous kernel's tail.  For calls long enough to repay it, each CTA cuts the
+ *     work from a first read of the lengths and prefetches its warps' first chunks
+ *     into L2 before griddepcontrol.wait (L2-only accesses; lengths, table and K/V
+ *     are read again after the wait); nothing else touches global memory before the
+ *     previous kernel completes.
  */
 #include <cuda.h>
 #include <cuda_bf16.h>
