@@ -99,6 +99,7 @@ struct DecodeParams {
     float scale_log2;    // scale * log2(e)
     int32_t min_chunks;
     int32_t spec_chunks;     // chunks per warp prefetched into L2 before griddepcontrol.wait
+    int64_t spec_min_total;  // ... only when the call has at least this many chunks in all
     int32_t debug_spec_skew; // test hook: added to every length the speculative pass reads
     int32_t debug_stuck;     // test hook: CTA 0 / warp 0 first stage expects 16 bytes too many
     uint64_t wait_limit_ns;  // bound on every mbarrier wait
@@ -344,7 +345,8 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
         scan_prefix([&](int b) { return ptx::ld_cg_s32(p.seq_lens + b) + p.debug_spec_skew; });
         const int64_t T = (int64_t)pre[p.B] * p.U;
         const int64_t nct = T > 0 ? active_ctas(T, gridDim.x, W, p.min_chunks) : 0;
-        if ((int64_t)blockIdx.x < nct) {
+        // the table may be far longer than the sequences: the prefetch needs real length
+        if ((int64_t)blockIdx.x < nct && T >= p.spec_min_total) {
             const int64_t cs = slice_begin(blockIdx.x, nct, T);
             const int64_t clen = slice_begin(blockIdx.x + 1, nct, T) - cs;
             const int wa = (int)active_warps(clen, W);
@@ -1150,15 +1152,21 @@ const Knobs& knobs() {
 // chunks per warp prefetched into L2 before griddepcontrol.wait (bf16 / e4m3 pools)
 constexpr int kDefaultSpecChunks = 4;
 constexpr int kDefaultSpecChunksKv8 = 4;
-// The pass before griddepcontrol.wait is run only when a warp streams at least this many
-// chunks at the table's capacity: it hides behind a previous decode grid's tail, but a
-// call with nothing ahead of it pays its ~2 us in full, which only a long stream repays.
+// The pass before griddepcontrol.wait runs only when a warp streams at least this many
+// chunks: it hides behind a previous decode grid's tail, but a call with nothing ahead of
+// it pays its ~2 us in full, which only a long stream repays.  The host checks the table's
+// capacity (the pass is then left out entirely); the kernel checks the real lengths
+// before it reads the table and prefetches.
 constexpr int64_t kSpecMinChunksPerWarp = 8;
+
+int64_t spec_min_total_for(const pgqa_plan& plan) {
+    return kSpecMinChunksPerWarp * plan.grid_ctas * plan.warps_per_cta;
+}
 
 int spec_chunks_for(int64_t B, const pgqa_plan& plan, int64_t cap_tokens, bool kv8) {
     if (knobs().spec >= 0) return knobs().spec;
     const int64_t chunks = B * plan.units_per_seq * ((cap_tokens + kChunkTokens - 1) / kChunkTokens);
-    if (chunks < kSpecMinChunksPerWarp * plan.grid_ctas * plan.warps_per_cta) return 0;
+    if (chunks < spec_min_total_for(plan)) return 0;
     return kv8 ? kDefaultSpecChunksKv8 : kDefaultSpecChunks;
 }
 
@@ -1542,6 +1550,8 @@ int decode_impl(const void* q, const void* k, const void* v, void* out, const in
     p.debug_stuck = env_int("PGQA_DEBUG_STUCK_BARRIER", 0) != 0;
     p.debug_spec_skew = env_int("PGQA_DEBUG_SPEC_SKEW", 0);
     p.spec_chunks = spec_chunks_for(B, plan, cap, kv8);
+    // The sweep knob and the test hook run the whole pass whatever the size of the call.
+    p.spec_min_total = (knobs().spec >= 0 || p.debug_spec_skew != 0) ? 0 : spec_min_total_for(plan);
     if (p.debug_spec_skew != 0 && p.spec_chunks == 0) p.spec_chunks = kDefaultSpecChunks;
     {
         const char* lim = getenv("PGQA_WAIT_LIMIT_NS");
