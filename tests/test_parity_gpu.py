@@ -207,6 +207,44 @@ def test_speculative_prefix_is_rebuilt_when_lengths_change(skew, cuda_device, mo
     assert torch.equal(out, plain)
 
 
+@pytest.mark.parametrize("kind", ["fp8", "multi_token_append"])
+def test_speculative_pass_on_other_instantiations(kind, cuda_device, monkeypatch):
+    """The same forced pass (PGQA_DEBUG_SPEC_SKEW) on e4m3 pages (two prefetch boxes a
+    chunk) and on a causal two-token decode that appends its new tokens first (the pass
+    reads lengths plus the appended count while the append may still be running)."""
+    from oracle import append_kv_ref, paged_decode_fp8_ref
+    lens = [1, 17, 300, 2048, 33]
+    if kind == "fp8":
+        f8 = inputs.to_fp8(inputs.custom_case(5, 32, 4, 16, lens, seed=43))
+        d = f8.to(cuda_device)
+        ref = paged_decode_fp8_ref(f8.q, f8.k, f8.v, f8.k_scale, f8.v_scale, f8.block_table,
+                                   f8.seq_lens)
+        call = lambda ws=None: pgqa.decode(d.q, d.k, d.v, d.block_table, d.seq_lens,
+                                           k_scale=d.k_scale, v_scale=d.v_scale, workspace=ws)
+    else:
+        base = inputs.custom_case(5, 32, 4, 16, [L + 2 for L in lens], seed=44)
+        base.seq_lens = torch.tensor(lens, dtype=torch.int32)
+        g = torch.Generator().manual_seed(45)
+        q2 = torch.randn(5, 2, 32, 128, generator=g).to(torch.bfloat16)
+        kn = torch.randn(5, 2, 4, 128, generator=g).to(torch.bfloat16)
+        vn = torch.randn(5, 2, 4, 128, generator=g).to(torch.bfloat16)
+        ek, ev = append_kv_ref(base.k, base.v, kn, vn, base.seq_lens, base.block_table)
+        ref = paged_decode_ref(q2, ek, ev, base.block_table, base.seq_lens + 2, causal=True)
+
+        def call(ws=None):
+            d = base.to(cuda_device)  # a fresh pool: the call appends into it
+            return pgqa.decode(q2.to(cuda_device), d.k, d.v, d.block_table, d.seq_lens,
+                               causal=True, k_new=kn.to(cuda_device), v_new=vn.to(cuda_device),
+                               workspace=ws)
+    plain = call()
+    monkeypatch.setenv("PGQA_DEBUG_SPEC_SKEW", "16")
+    ws = ops.workspace_for(5, 32, 4, 128, 16, cuda_device, seqlen_q=1 if kind == "fp8" else 2)
+    out = call(ws)
+    pgqa.check_device_error(ws)
+    assert_parity(out, ref, what=f"{kind} with the forced pass")
+    assert torch.equal(out, plain)
+
+
 def test_custom_scale(cuda_device):
     inp = inputs.custom_case(3, 16, 2, 16, [7, 70, 700], seed=21)
     d = inp.to(cuda_device)
