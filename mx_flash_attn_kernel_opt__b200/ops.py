@@ -215,6 +215,57 @@ def run_kernel(q, k_cache_paged, v_cache_paged, output, cache_seqlens, block_tab
     return output
 
 
+def flash_attn_with_kvcache(q, k_cache, v_cache, k=None, v=None, rotary_cos=None,
+                            rotary_sin=None, cache_seqlens=None, cache_batch_idx=None,
+                            cache_leftpad=None, block_table=None, softmax_scale=None,
+                            causal=False, window_size=(-1, -1), softcap=0.0,
+                            rotary_interleaved=True, alibi_slopes=None, num_splits=0,
+                            return_softmax_lse=False):
+    """flash_attn.flash_attn_with_kvcache's argument list (flash-attn 2.8), the operator the
+    reference is benchmarked against (task.md:16-26), for the case this library runs: a
+    paged cache (`block_table`), per-sequence lengths `cache_seqlens` (int or [B] int32),
+    optional new tokens `k` / `v` [B, S_new, Hkv, D] written into the cache in place at
+    positions [cache_seqlens[b], cache_seqlens[b] + S_new) first, and the end-aligned
+    causal mask.  q is [B, Sq, Hq, D]; returns out of q's shape.  `num_splits` is accepted
+    and ignored (the split follows the real lengths on the device); `rotary_interleaved`
+    only matters with rotary inputs.  Every other option raises NotImplementedError
+    instead of being ignored.
+    """
+    unsupported = []
+    if rotary_cos is not None or rotary_sin is not None:
+        unsupported.append("rotary embedding (rotary_cos / rotary_sin)")
+    if cache_batch_idx is not None:
+        unsupported.append("cache_batch_idx")
+    if cache_leftpad is not None:
+        unsupported.append("cache_leftpad")
+    if tuple(window_size) != (-1, -1):
+        unsupported.append("window_size (local attention)")
+    if softcap:
+        unsupported.append("softcap")
+    if alibi_slopes is not None:
+        unsupported.append("alibi_slopes")
+    if return_softmax_lse:
+        unsupported.append("return_softmax_lse")
+    if block_table is None:
+        unsupported.append("a non-paged cache (block_table=None)")
+    if unsupported:
+        raise NotImplementedError("flash_attn_with_kvcache: not implemented here: "
+                                  + ", ".join(unsupported))
+    if q.dim() != 4:
+        raise ValueError("flash_attn_with_kvcache: q must be [B, Sq, Hq, D]")
+    if (k is None) != (v is None):
+        raise ValueError("flash_attn_with_kvcache: give both k and v, or neither")
+    B = q.shape[0]
+    if cache_seqlens is None:
+        raise ValueError("flash_attn_with_kvcache: cache_seqlens is required with a paged cache")
+    if isinstance(cache_seqlens, int):
+        cache_seqlens = torch.full((B,), cache_seqlens, dtype=torch.int32, device=q.device)
+    elif cache_seqlens.dtype != torch.int32:
+        cache_seqlens = cache_seqlens.to(torch.int32)
+    return decode(q, k_cache, v_cache, block_table, cache_seqlens, scale=softmax_scale,
+                  causal=bool(causal), k_new=k, v_new=v)
+
+
 def run_kernel_cabi(q, k_cache_paged, v_cache_paged, output, cache_seqlens, block_table,
                     batch_size, seqlen_k, seqlen_q, num_heads, num_heads_k, headdim,
                     page_block_size, num_blocks, causal):

@@ -64,3 +64,32 @@ def test_matches_flash_attn_with_kvcache(Sq, S_new, causal, Hq, Hkv, cuda_device
     if S_new:
         assert torch.equal(d.k.view(torch.int16), k_fa.view(torch.int16))
         assert torch.equal(d.v.view(torch.int16), v_fa.view(torch.int16))
+
+
+@pytest.mark.parametrize("Sq,S_new,causal", [(1, 0, False), (4, 4, True)])
+def test_same_call_through_both_libraries(Sq, S_new, causal, cuda_device):
+    """pgqa.flash_attn_with_kvcache takes flash-attn's own argument list: the same keyword
+    arguments go to both libraries, each on its own copy of the cache."""
+    fa = _fa()
+    lens = [1, 300, 4000]
+    inp, q, kn, vn = _case(lens, S_new, Sq, 32, 8, seed=71 + Sq)
+    d = inp.to(cuda_device)
+    kw = dict(cache_seqlens=d.seq_lens, block_table=d.block_table, softmax_scale=inp.scale,
+              causal=causal, num_splits=0)
+    if S_new:
+        kw.update(k=kn.to(cuda_device), v=vn.to(cuda_device))
+    qd = q.to(cuda_device)
+    k_fa, v_fa = d.k.clone(), d.v.clone()
+    try:
+        ref = fa(qd, k_fa, v_fa, **kw)
+        torch.cuda.synchronize(cuda_device)
+    except RuntimeError as e:
+        pytest.skip(f"flash_attn_with_kvcache did not run here: {e}")
+    out = pgqa.flash_attn_with_kvcache(qd, d.k, d.v, **kw)
+    torch.cuda.synchronize(cuda_device)
+    assert out.shape == ref.shape
+    assert torch.allclose(out.float(), ref.float(), atol=ATOL, rtol=RTOL), \
+        f"max |diff| {(out.float() - ref.float()).abs().max().item()}"
+    if S_new:
+        assert torch.equal(d.k.view(torch.int16), k_fa.view(torch.int16))
+        assert torch.equal(d.v.view(torch.int16), v_fa.view(torch.int16))
