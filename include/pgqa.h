@@ -152,6 +152,42 @@ int pgqa_decode_fp8(const void* q, void* k_cache, void* v_cache, const void* k_n
                     int64_t causal, float scale, const float* k_scale, const float* v_scale,
                     void* workspace, size_t workspace_bytes, void* stream);
 
+/*
+ * Every option in one call, with an optional log-sum-exp output (no counterpart in the
+ * reference; flash_attn_with_kvcache's return_softmax_lse).  Fields not named below are
+ * those of pgqa_decode_fp8 / pgqa_decode_kvcache, with the same meaning and checks.
+ *   struct_size  sizeof(pgqa_decode_args) as the caller was compiled (checked)
+ *   kv_format    0: bf16 pools (k_scale / v_scale must be NULL), 1: e4m3 pools
+ *   softmax_lse  NULL, or fp32 [batch_size, num_heads, seqlen_q]: ln of the sum of
+ *                exp(scale * q.k) over the keys each query row sees (-inf for a row that
+ *                sees none).  Compiled for the default launch shape only: under the
+ *                PGQA_WARPS / PGQA_STAGES sweep knobs a call asking for it returns
+ *                PGQA_ERR_UNSUPPORTED.
+ * The workspace size is pgqa_workspace_size_v2's; workspace NULL uses the library's.
+ */
+typedef struct pgqa_decode_args {
+    size_t struct_size;
+    const void* q;
+    void* k_cache;
+    void* v_cache;
+    const void* k_new;
+    const void* v_new;
+    void* out;
+    float* softmax_lse;
+    const int32_t* seq_lens;
+    const int32_t* block_table;
+    int64_t batch_size, seqlen_q, seqlen_new, num_heads, num_heads_k, headdim;
+    int64_t page_size, num_pages, bt_stride, max_seqlen, causal;
+    float scale;
+    int32_t kv_format;
+    const float* k_scale;
+    const float* v_scale;
+    void* workspace;
+    size_t workspace_bytes;
+} pgqa_decode_args;
+
+int pgqa_decode_ex(const pgqa_decode_args* args, void* stream);
+
 /* pgqa_append_kv for e4m3 pools (128-byte token rows). */
 int pgqa_append_kv_fp8(const void* k_new, const void* v_new, void* k_cache, void* v_cache,
                        const int32_t* seq_lens, const int32_t* block_table, int64_t batch_size,

@@ -36,6 +36,23 @@ class PgqaPlan(ctypes.Structure):
         return {name: getattr(self, name) for name, _ in self._fields_}
 
 
+class PgqaDecodeArgs(ctypes.Structure):
+    """include/pgqa.h pgqa_decode_args (pgqa_decode_ex)."""
+    _fields_ = [
+        ("struct_size", c_size_t),
+        ("q", c_void_p), ("k_cache", c_void_p), ("v_cache", c_void_p),
+        ("k_new", c_void_p), ("v_new", c_void_p), ("out", c_void_p),
+        ("softmax_lse", c_void_p), ("seq_lens", c_void_p), ("block_table", c_void_p),
+        ("batch_size", c_int64), ("seqlen_q", c_int64), ("seqlen_new", c_int64),
+        ("num_heads", c_int64), ("num_heads_k", c_int64), ("headdim", c_int64),
+        ("page_size", c_int64), ("num_pages", c_int64), ("bt_stride", c_int64),
+        ("max_seqlen", c_int64), ("causal", c_int64),
+        ("scale", c_float), ("kv_format", ctypes.c_int32),
+        ("k_scale", c_void_p), ("v_scale", c_void_p),
+        ("workspace", c_void_p), ("workspace_bytes", c_size_t),
+    ]
+
+
 SIGNATURES = {
     "run_kernel": (None, [c_void_p] * 4 + [c_void_p, c_void_p] + [c_int64] * 9),
     "pgqa_decode_v1": (ctypes.c_int, [c_void_p] * 6 + [c_int64] * 8 +
@@ -43,6 +60,7 @@ SIGNATURES = {
     "pgqa_decode_noalloc": (ctypes.c_int, [c_void_p] * 6 + [c_int64] * 8 + [c_float, c_void_p]),
     "pgqa_decode_v2": (ctypes.c_int, [c_void_p] * 6 + [c_int64] * 10 +
                        [c_float, c_void_p, c_size_t, c_void_p]),
+    "pgqa_decode_ex": (ctypes.c_int, [ctypes.POINTER(PgqaDecodeArgs), c_void_p]),
     "pgqa_workspace_size_v2": (c_size_t, [c_int64] * 6),
     "pgqa_append_kv": (ctypes.c_int, [c_void_p] * 6 + [c_int64] * 7 + [c_void_p] * 2),
     "pgqa_decode_kvcache": (ctypes.c_int, [c_void_p] * 8 + [c_int64] * 11 +

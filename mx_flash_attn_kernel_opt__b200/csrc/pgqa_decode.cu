@@ -79,6 +79,7 @@ static_assert(kErrBadPage == kAppendBadPage && kErrBadSeqlen == kAppendBadSeqlen
 struct DecodeParams {
     const __nv_bfloat16* q;
     __nv_bfloat16* out;
+    float* lse_out;      // optional [B, Hq, Sq] fp32 natural-log sum-exp per query row
     const int32_t* seq_lens;
     const int32_t* block_table;
     float* rec_o;        // [2 * grid * NG][8 M tiles][32 lanes] float4 (O^T fragments)
@@ -214,6 +215,26 @@ __device__ __forceinline__ int64_t row_offset(const DecodeParams& p, int32_t b, 
     return (((int64_t)b * p.Sq + i) * p.Hq + kvh * p.g + h) * kHeadDim;
 }
 
+/* Index of query row r of KV head kvh, sequence b, in the [B, Hq, Sq] log-sum-exp output. */
+template <bool MQ>
+__device__ __forceinline__ int64_t lse_index(const DecodeParams& p, int32_t b, int32_t kvh, int r) {
+    if (!MQ) return (int64_t)b * p.Hq + kvh * p.g + r;  // Sq == 1
+    const int h = r / p.Sq;
+    const int i = r - h * p.Sq;
+    return ((int64_t)b * p.Hq + kvh * p.g + h) * p.Sq + i;
+}
+
+/* Writes the natural-log sum-exp of this lane's two rows 2tig, 2tig+1 of row group hg
+ * from their log2-domain values (lanes with gid == 0 call it; rows past nhv are padding). */
+template <bool MQ>
+__device__ __forceinline__ void store_lse(const DecodeParams& p, int32_t b, int32_t kvh, int hg,
+                                          int nhv, int tig, float lse2A, float lse2B) {
+    constexpr float kLn2 = 0.6931471805599453f;
+    const int r = 2 * tig;
+    if (r < nhv) p.lse_out[lse_index<MQ>(p, b, kvh, hg * kHeadsPerGroup + r)] = lse2A * kLn2;
+    if (r + 1 < nhv) p.lse_out[lse_index<MQ>(p, b, kvh, hg * kHeadsPerGroup + r + 1)] = lse2B * kLn2;
+}
+
 /* Keys visible to query row r of a sequence of length L. */
 template <bool MQ>
 __device__ __forceinline__ int32_t row_limit(const DecodeParams& p, int r, int32_t L) {
@@ -263,7 +284,7 @@ struct PairMerge {
  * KV8 = true: e4m3 pools, 4 KB stages (one 128-byte box each for K and V); the fp8
  * bytes are converted exactly to f16 after ldmatrix and multiplied with f16 MMAs
  * (q rounded to f16 after an exact per-row power-of-two rescale; P in f16). */
-template <int W, int S, bool MQ, bool KV8, int NG>
+template <int W, int S, bool MQ, bool KV8, int NG, bool LSE>
 __global__ void __launch_bounds__(W * 32, 1)
 pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
                    const __grid_constant__ CUtensorMap vmap, const DecodeParams p) {
@@ -875,6 +896,9 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
                             for (int mt = 0; mt < 8; ++mt)
                                 store_tile<KV8>(orow, o[gr][mt][0], o[gr][mt][1], o[gr][mt][2],
                                                 o[gr][mt][3], invA, invB, mt, tig, gid < nh_valid[gr]);
+                            if (LSE && gid == 0)
+                                store_lse<MQ>(p, cc.b, kvh, hg, nh_valid[gr], tig,
+                                              m2[gr][0] + ptx::lg2(lA), m2[gr][1] + ptx::lg2(lB));
                         }
                     } else {
                         const float lseA = m2[gr][0] + ptx::lg2(lA);
@@ -1055,6 +1079,8 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
             const float invB = (!MQ || dB > 0.f) ? 1.f / dB : 0.f;
             if (inside) {
                 store_tile<KV8>(orow, a0, a1, a2, a3, invA, invB, mt, tig, gid < nhv);
+                if (LSE && mt == 0 && gid == 0)
+                    store_lse<MQ>(p, ub, kvh, hg, nhv, tig, bA + ptx::lg2(dA), bB + ptx::lg2(dB));
                 continue;
             }
             const int64_t slot = record_slot(blockIdx.x, cs, ubeg) * NG + gq;
@@ -1111,6 +1137,8 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
             }
             store_tile<KV8>(orow, g.a0, g.a1, g.a2, g.a3, (!MQ || g.dA > 0.f) ? 1.f / g.dA : 0.f,
                            (!MQ || g.dB > 0.f) ? 1.f / g.dB : 0.f, mt, tig, gid < nhv);
+            if (LSE && mt == 0 && gid == 0)
+                store_lse<MQ>(p, ub, kvh, hg, nhv, tig, g.mA + ptx::lg2(g.dA), g.mB + ptx::lg2(g.dB));
         }
     }
 }
@@ -1387,10 +1415,10 @@ int lib_workspace(int dev, size_t need, void** out) {
     return PGQA_OK;
 }
 
-template <int W, int S, bool MQ, bool KV8, int NG>
+template <int W, int S, bool MQ, bool KV8, int NG, bool LSE = false>
 int launch_variant(const CUtensorMap& km, const CUtensorMap& vm, const DecodeParams& p, int grid,
                    int smem, cudaStream_t stream) {
-    auto kern = pgqa_decode_kernel<W, S, MQ, KV8, NG>;
+    auto kern = pgqa_decode_kernel<W, S, MQ, KV8, NG, LSE>;
     static int configured_smem[kMaxDevices] = {0};  // one table per instantiation
     int dev = 0;
     cudaGetDevice(&dev);
@@ -1425,6 +1453,14 @@ int launch_t(const pgqa_plan& plan, const CUtensorMap& km, const CUtensorMap& vm
              const DecodeParams& p, cudaStream_t stream) {
     const int w = plan.warps_per_cta, s = plan.stages;
     const int g = plan.grid_ctas, sm = plan.smem_bytes;
+    if (p.lse_out != nullptr) {
+        // the log-sum-exp output is compiled for the default rings only (8 warps; bf16
+        // 2 stages, e4m3 4) so that no other instantiation carries its code
+        if (w != 8 || s != (KV8 ? 4 : 2)) return PGQA_ERR_UNSUPPORTED;
+        if (plan.groups_per_unit == 2)
+            return launch_variant<8, KV8 ? 4 : 2, MQ, KV8, 2, true>(km, vm, p, g, sm, stream);
+        return launch_variant<8, KV8 ? 4 : 2, MQ, KV8, 1, true>(km, vm, p, g, sm, stream);
+    }
     if (plan.groups_per_unit == 2) {
         if (KV8 && w == 8 && s == 4) return launch_variant<8, 4, MQ, true, 2>(km, vm, p, g, sm, stream);
         if (!KV8 && w == 8 && s == 2) return launch_variant<8, 2, MQ, false, 2>(km, vm, p, g, sm, stream);
@@ -1463,7 +1499,7 @@ int decode_impl(const void* q, const void* k, const void* v, void* out, const in
                 int64_t causal, float scale, void* workspace, size_t ws_bytes,
                 cudaStream_t stream, const void* k_new = nullptr, const void* v_new = nullptr,
                 int64_t len_add = 0, bool kv8 = false, const float* k_scale = nullptr,
-                const float* v_scale = nullptr) {
+                const float* v_scale = nullptr, float* lse_out = nullptr) {
     if (!q || !k || !v || !out || !seq_lens || !bt) return PGQA_ERR_NULL_POINTER;
     if (len_add < 0 || len_add > 4096) return len_add < 0 ? PGQA_ERR_BAD_SHAPE : PGQA_ERR_UNSUPPORTED;
     if (len_add > 0 && (!k_new || !v_new)) return PGQA_ERR_NULL_POINTER;
@@ -1521,6 +1557,7 @@ int decode_impl(const void* q, const void* k, const void* v, void* out, const in
     p.counters = reinterpret_cast<int32_t*>(ws + off);
     p.q = static_cast<const __nv_bfloat16*>(q);
     p.out = static_cast<__nv_bfloat16*>(out);
+    p.lse_out = lse_out;
     p.seq_lens = seq_lens;
     p.block_table = bt;
     p.B = (int32_t)B;
@@ -1745,6 +1782,22 @@ extern "C" int pgqa_decode_fp8(const void* q, void* k_cache, void* v_cache, cons
                                   bt_stride, max_seqlen, causal, scale, workspace,
                                   workspace_bytes, static_cast<cudaStream_t>(stream), k_new,
                                   v_new, seqlen_new, true, k_scale, v_scale));
+}
+
+extern "C" int pgqa_decode_ex(const pgqa_decode_args* a, void* stream) {
+    if (a == nullptr) return set_status(PGQA_ERR_NULL_POINTER);
+    if (a->struct_size != sizeof(pgqa_decode_args)) return set_status(PGQA_ERR_BAD_SHAPE);
+    if (a->kv_format != 0 && a->kv_format != 1) return set_status(PGQA_ERR_UNSUPPORTED);
+    if (a->kv_format == 0 && (a->k_scale != nullptr || a->v_scale != nullptr))
+        return set_status(PGQA_ERR_BAD_SHAPE);  // scales describe e4m3 pools only
+    if (reinterpret_cast<uintptr_t>(a->softmax_lse) & 3) return set_status(PGQA_ERR_MISALIGNED);
+    return set_status(decode_impl(a->q, a->k_cache, a->v_cache, a->out, a->seq_lens,
+                                  a->block_table, a->batch_size, a->seqlen_q, a->num_heads,
+                                  a->num_heads_k, a->headdim, a->page_size, a->num_pages,
+                                  a->bt_stride, a->max_seqlen, a->causal, a->scale, a->workspace,
+                                  a->workspace_bytes, static_cast<cudaStream_t>(stream),
+                                  a->k_new, a->v_new, a->seqlen_new, a->kv_format == 1,
+                                  a->k_scale, a->v_scale, a->softmax_lse));
 }
 
 static size_t workspace_size_impl(int64_t batch_size, int64_t seqlen_q, int64_t num_heads,

@@ -17,7 +17,7 @@ import math
 
 import torch
 
-from ._lib import PgqaError, PgqaPlan, check, lib
+from ._lib import PgqaDecodeArgs, PgqaError, PgqaPlan, check, lib
 
 _workspaces = {}
 
@@ -80,7 +80,7 @@ def _scale_array(x, Hkv, device):
 
 def decode(q, k_cache, v_cache, block_table, seq_lens, scale=None, out=None,
            max_seqlen=0, workspace=None, causal=False, k_new=None, v_new=None,
-           k_scale=None, v_scale=None):
+           k_scale=None, v_scale=None, return_lse=False):
     """Paged GQA decode.
 
     q [B, Hq, D] (one query token) or [B, Sq, Hq, D] bf16; k_cache/v_cache
@@ -93,7 +93,9 @@ def decode(q, k_cache, v_cache, block_table, seq_lens, scale=None, out=None,
     the lengths before the append and is not modified).
 
     FP8 pools: an element of KV head h is worth e4m3 * k_scale[h] (v_scale for V);
-    k_scale / v_scale are floats or [Hkv] tensors (None = 1).  Returns out (q's shape).
+    k_scale / v_scale are floats or [Hkv] tensors (None = 1).  Returns out (q's shape),
+    or (out, lse) with `return_lse`: lse [B, Hq, Sq] fp32, the natural log of the sum of
+    exp(scale * q.k) over the keys each query row sees (-inf for a row that sees none).
     """
     if out is None:
         out = torch.empty_like(q)
@@ -122,6 +124,25 @@ def decode(q, k_cache, v_cache, block_table, seq_lens, scale=None, out=None,
     if workspace is None:
         workspace = workspace_for(B, Hq, Hkv, D, P, q.device, seqlen_q=Sq)
     L = lib()
+    if return_lse:
+        lse = torch.empty(B, Hq, Sq, dtype=torch.float32, device=q.device)
+        ks = _scale_array(k_scale, Hkv, q.device) if fp8 else None
+        vs = _scale_array(v_scale, Hkv, q.device) if fp8 else None
+        a = PgqaDecodeArgs(
+            struct_size=ctypes.sizeof(PgqaDecodeArgs), q=_ptr(q), k_cache=_ptr(k_cache),
+            v_cache=_ptr(v_cache), k_new=_ptr(k_new) if S_new else None,
+            v_new=_ptr(v_new) if S_new else None, out=_ptr(out), softmax_lse=_ptr(lse),
+            seq_lens=_ptr(seq_lens), block_table=_ptr(block_table), batch_size=B,
+            seqlen_q=Sq, seqlen_new=S_new, num_heads=Hq, num_heads_k=Hkv, headdim=D,
+            page_size=P, num_pages=num_pages, bt_stride=block_table.stride(0),
+            max_seqlen=max_seqlen, causal=int(bool(causal)), scale=float(scale),
+            kv_format=1 if fp8 else 0, k_scale=_ptr(ks) if ks is not None else None,
+            v_scale=_ptr(vs) if vs is not None else None, workspace=_ptr(workspace),
+            workspace_bytes=workspace.numel())
+        with torch.cuda.device(q.device):
+            st = L.pgqa_decode_ex(ctypes.byref(a), _stream_handle(q.device))
+        check(st, "pgqa_decode_ex")
+        return out, lse
     with torch.cuda.device(q.device):
         if fp8:
             ks = _scale_array(k_scale, Hkv, q.device)
@@ -226,7 +247,8 @@ def flash_attn_with_kvcache(q, k_cache, v_cache, k=None, v=None, rotary_cos=None
     paged cache (`block_table`), per-sequence lengths `cache_seqlens` (int or [B] int32),
     optional new tokens `k` / `v` [B, S_new, Hkv, D] written into the cache in place at
     positions [cache_seqlens[b], cache_seqlens[b] + S_new) first, and the end-aligned
-    causal mask.  q is [B, Sq, Hq, D]; returns out of q's shape.  `num_splits` is accepted
+    causal mask.  q is [B, Sq, Hq, D]; returns out of q's shape, or (out, softmax_lse
+    [B, Hq, Sq] fp32) with `return_softmax_lse`, as flash-attn does.  `num_splits` is accepted
     and ignored (the split follows the real lengths on the device); `rotary_interleaved`
     only matters with rotary inputs.  Every other option raises NotImplementedError
     instead of being ignored.
@@ -244,8 +266,6 @@ def flash_attn_with_kvcache(q, k_cache, v_cache, k=None, v=None, rotary_cos=None
         unsupported.append("softcap")
     if alibi_slopes is not None:
         unsupported.append("alibi_slopes")
-    if return_softmax_lse:
-        unsupported.append("return_softmax_lse")
     if block_table is None:
         unsupported.append("a non-paged cache (block_table=None)")
     if unsupported:
@@ -263,7 +283,7 @@ def flash_attn_with_kvcache(q, k_cache, v_cache, k=None, v=None, rotary_cos=None
     elif cache_seqlens.dtype != torch.int32:
         cache_seqlens = cache_seqlens.to(torch.int32)
     return decode(q, k_cache, v_cache, block_table, cache_seqlens, scale=softmax_scale,
-                  causal=bool(causal), k_new=k, v_new=v)
+                  causal=bool(causal), k_new=k, v_new=v, return_lse=bool(return_softmax_lse))
 
 
 def run_kernel_cabi(q, k_cache_paged, v_cache_paged, output, cache_seqlens, block_table,

@@ -34,7 +34,7 @@ def _gather_seq(k_cache, v_cache, block_table, b, L):
 
 
 def paged_decode_ref(q, k_cache, v_cache, block_table, seq_lens, scale=None, rows=None,
-                     causal=False):
+                     causal=False, return_lse=False):
     """fp32 reference.  q [B, Hq, D] (one query token) or [B, Sq, Hq, D]; pools
     [num_pages, P, Hkv, D].  Returns fp32 of q's shape.
 
@@ -42,7 +42,9 @@ def paged_decode_ref(q, k_cache, v_cache, block_table, seq_lens, scale=None, row
     keys [0, L_b - Sq + i] (the mask aligned to the end of the cache, as
     flash_attn_with_kvcache defines it).  A query with no visible key (L_b == 0, or
     causal with L_b - Sq + i < 0) gives zeros.  `rows` limits the work to the given
-    sequence indices (the other rows stay zero)."""
+    sequence indices (the other rows stay zero).  With `return_lse` also returns
+    lse [B, Hq, Sq] fp32: ln of the sum of exp(scale * q.k) over the visible keys (-inf
+    for a query with none), as flash_attn_with_kvcache's softmax_lse."""
     squeeze = q.dim() == 3
     q4 = (q.unsqueeze(1) if squeeze else q).cpu()
     k_cache, v_cache = k_cache.cpu(), v_cache.cpu()
@@ -53,6 +55,7 @@ def paged_decode_ref(q, k_cache, v_cache, block_table, seq_lens, scale=None, row
     if scale is None:
         scale = 1.0 / math.sqrt(D)
     out = torch.zeros(B, Sq, Hq, D, dtype=torch.float32)
+    lse = torch.full((B, Hq, Sq), float("-inf"), dtype=torch.float32)
     for b in (range(B) if rows is None else rows):
         L = int(seq_lens[b])
         if L <= 0:
@@ -68,11 +71,13 @@ def paged_decode_ref(q, k_cache, v_cache, block_table, seq_lens, scale=None, row
             s = torch.bmm(qb, Kt[:, :, :n]) * scale    # [Hkv, g, n]
             p = torch.softmax(s, dim=-1)
             out[b, i] = torch.bmm(p, Vt[:, :n]).reshape(Hq, D)
-    return out[:, 0] if squeeze else out
+            lse[b, :, i] = torch.logsumexp(s, dim=-1).reshape(Hq)
+    out = out[:, 0] if squeeze else out
+    return (out, lse) if return_lse else out
 
 
 def paged_decode_fp8_ref(q, k8, v8, k_scale, v_scale, block_table, seq_lens, scale=None,
-                         causal=False):
+                         causal=False, return_lse=False):
     """FP8 KV pages: the value of an element of KV head h is e4m3 * k_scale[h]
     (v_scale[h] for V).  The e4m3 bytes are decoded by torch's float8_e4m3fn conversion
     (OCP e4m3fn: bias 7, NaN = S.1111.111, no infinities), dequantised in fp32 and fed
@@ -82,7 +87,8 @@ def paged_decode_fp8_ref(q, k8, v8, k_scale, v_scale, block_table, seq_lens, sca
     vs = torch.as_tensor(v_scale, dtype=torch.float32).reshape(-1).expand(Hkv).cpu()
     kd = k8.cpu().float() * ks.view(1, 1, Hkv, 1)
     vd = v8.cpu().float() * vs.view(1, 1, Hkv, 1)
-    return paged_decode_ref(q, kd, vd, block_table, seq_lens, scale=scale, causal=causal)
+    return paged_decode_ref(q, kd, vd, block_table, seq_lens, scale=scale, causal=causal,
+                            return_lse=return_lse)
 
 
 LOG2E = 1.4426950408889634

@@ -104,6 +104,52 @@ def test_extended_entry_validates_arguments():
     assert _lib.lib().pgqa_last_status() == 4
 
 
+def _ex_args(**kw):
+    a = _lib.PgqaDecodeArgs(
+        struct_size=ctypes.sizeof(_lib.PgqaDecodeArgs), q=0x10000, k_cache=0x20000,
+        v_cache=0x30000, out=0x40000, seq_lens=0x50000, block_table=0x60000, batch_size=2,
+        seqlen_q=1, num_heads=32, num_heads_k=8, headdim=128, page_size=16, num_pages=8,
+        bt_stride=4, scale=0.088, kv_format=0)
+    for k, v in kw.items():
+        setattr(a, k, v)
+    return a
+
+
+def test_struct_entry_validates_arguments():
+    """pgqa_decode_ex checks its struct before anything else (no device needed)."""
+    L = _lib.lib()
+    assert L.pgqa_decode_ex(None, None) == 1
+    assert L.pgqa_decode_ex(ctypes.byref(_ex_args(struct_size=8)), None) == 2
+    assert L.pgqa_decode_ex(ctypes.byref(_ex_args(kv_format=2)), None) == 3
+    assert L.pgqa_decode_ex(ctypes.byref(_ex_args(k_scale=0x70000)), None) == 2
+    assert L.pgqa_decode_ex(ctypes.byref(_ex_args(softmax_lse=0x70002)), None) == 4
+    assert L.pgqa_decode_ex(ctypes.byref(_ex_args(batch_size=0)), None) == 2
+    assert L.pgqa_decode_ex(ctypes.byref(_ex_args(q=None)), None) == 1
+    assert L.pgqa_last_status() == 1
+
+
+def test_struct_layout_matches_the_header(tmp_path):
+    """The ctypes mirror of pgqa_decode_args has the C struct's size and field offsets
+    (a probe compiled with gcc against include/pgqa.h)."""
+    import shutil
+    if shutil.which("gcc") is None:
+        pytest.skip("gcc not available")
+    fields = [f for f, _ in _lib.PgqaDecodeArgs._fields_]
+    src = tmp_path / "probe.c"
+    src.write_text("#include <stdio.h>\n#include <stddef.h>\n#include \"pgqa.h\"\nint main(void) {\n"
+                   + '  printf("%zu\\n", sizeof(pgqa_decode_args));\n'
+                   + "".join(f'  printf("%zu\\n", offsetof(pgqa_decode_args, {f}));\n' for f in fields)
+                   + "  return 0;\n}\n")
+    exe = tmp_path / "probe"
+    cuda_inc = "/usr/local/cuda/include"
+    r = subprocess.run(["gcc", "-I", os.path.join(REPO, "include"), "-I", cuda_inc, str(src),
+                        "-o", str(exe)], capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    got = [int(x) for x in subprocess.run([str(exe)], capture_output=True, text=True).stdout.split()]
+    assert got[0] == ctypes.sizeof(_lib.PgqaDecodeArgs)
+    assert got[1:] == [getattr(_lib.PgqaDecodeArgs, f).offset for f in fields]
+
+
 @pytest.mark.skipif(torch.cuda.is_available(), reason="checks the no-device path")
 def test_valid_call_without_device_reports_no_device():
     assert _v1() == 7

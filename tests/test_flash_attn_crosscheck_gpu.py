@@ -87,6 +87,12 @@ def test_same_call_through_both_libraries(Sq, S_new, causal, cuda_device):
         pytest.skip(f"flash_attn_with_kvcache did not run here: {e}")
     out = pgqa.flash_attn_with_kvcache(qd, d.k, d.v, **kw)
     torch.cuda.synchronize(cuda_device)
+    if S_new == 0:  # the softmax_lse of the same call, from both libraries
+        _, lse_fa = fa(qd, d.k.clone(), d.v.clone(), return_softmax_lse=True, **kw)
+        _, lse = pgqa.flash_attn_with_kvcache(qd, d.k, d.v, return_softmax_lse=True, **kw)
+        assert lse.shape == lse_fa.shape
+        assert torch.allclose(lse, lse_fa.float(), atol=1e-3, rtol=1e-3), \
+            f"lse max |diff| {(lse - lse_fa.float()).abs().max().item()}"
     assert out.shape == ref.shape
     assert torch.allclose(out.float(), ref.float(), atol=ATOL, rtol=RTOL), \
         f"max |diff| {(out.float() - ref.float()).abs().max().item()}"

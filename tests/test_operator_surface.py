@@ -22,7 +22,6 @@ def _args(B=2, Sq=1, Hq=32, Hkv=8, P=16, pages=4):
     ("window_size", (64, 0)),
     ("softcap", 30.0),
     ("alibi_slopes", torch.zeros(32)),
-    ("return_softmax_lse", True),
 ])
 def test_unimplemented_options_raise(option, value):
     q, k, v, bt, lens = _args()
