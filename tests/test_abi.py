@@ -198,3 +198,41 @@ def test_plan_carries_two_row_groups_per_unit_when_a_kv_head_has_more():
     narrow = _lib.PgqaPlan()
     assert L.pgqa_make_plan(4, 32, 8, 128, 16, 148, 232448, ctypes.byref(narrow)) == 0
     assert (narrow.head_groups, narrow.groups_per_unit, narrow.units_per_seq) == (1, 1, 8)
+
+
+def test_a_c_program_builds_and_links_against_the_header(tmp_path):
+    """A C caller compiles against include/pgqa.h alone (no CUDA or torch headers), links
+    libpgqa.so and gets host-side answers: status strings, refused arguments, the struct
+    entry point's checks."""
+    import shutil
+    if shutil.which("gcc") is None:
+        pytest.skip("gcc not available")
+    src = tmp_path / "caller.c"
+    src.write_text(r"""
+#include <stdio.h>
+#include <string.h>
+#include "pgqa.h"
+int main(void) {
+    int fails = 0;
+    if (strlen(pgqa_status_string(PGQA_ERR_BAD_SHAPE)) == 0) fails++;
+    /* null pointers are refused before anything touches a device */
+    if (pgqa_decode_v1(0, 0, 0, 0, 0, 0, 2, 32, 8, 128, 16, 8, 4, 0, 0.088f, 0, 0, 0)
+        != PGQA_ERR_NULL_POINTER) fails++;
+    if (pgqa_last_status() != PGQA_ERR_NULL_POINTER) fails++;
+    pgqa_decode_args a;
+    memset(&a, 0, sizeof(a));
+    a.struct_size = sizeof(a) - 8;   /* a caller built against another layout */
+    if (pgqa_decode_ex(&a, 0) != PGQA_ERR_BAD_SHAPE) fails++;
+    if (pgqa_decode_ex(0, 0) != PGQA_ERR_NULL_POINTER) fails++;
+    printf("fails=%d\n", fails);
+    return fails;
+}
+""")
+    exe = tmp_path / "caller"
+    libdir = os.path.dirname(_lib.LIB_PATH)
+    r = subprocess.run(["gcc", "-std=c99", "-Wall", "-Werror", "-I", os.path.join(REPO, "include"),
+                        str(src), "-L", libdir, "-lpgqa", "-Wl,-rpath," + libdir, "-o", str(exe)],
+                       capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=120)
+    assert r.returncode == 0 and "fails=0" in r.stdout, r.stdout + r.stderr
