@@ -74,16 +74,25 @@ def test_lse_several_query_tokens(Sq, lens, cuda_device):
     assert_lse(lse, ref_lse, f"Sq={Sq}")
 
 
-def test_lse_fp8_pages(cuda_device):
+@pytest.mark.parametrize("Sq", [1, 3])
+def test_lse_fp8_pages(Sq, cuda_device):
+    """e4m3 pages, one token (one row group per unit) and three causal tokens (two row
+    groups per unit, the second partly padding; rows that see no key)."""
     f8 = inputs.to_fp8(inputs.custom_case(4, 32, 4, 16, [1, 300, 2048, 33], seed=61))
     d = f8.to(cuda_device)
-    ref, ref_lse = paged_decode_fp8_ref(f8.q, f8.k, f8.v, f8.k_scale, f8.v_scale,
-                                        f8.block_table, f8.seq_lens, return_lse=True)
-    out, lse = pgqa.decode(d.q, d.k, d.v, d.block_table, d.seq_lens, k_scale=d.k_scale,
-                           v_scale=d.v_scale, return_lse=True)
+    q = f8.q
+    if Sq > 1:
+        g = torch.Generator().manual_seed(64)
+        q = torch.randn(4, Sq, 32, 128, generator=g).to(torch.bfloat16)
+    ref, ref_lse = paged_decode_fp8_ref(q, f8.k, f8.v, f8.k_scale, f8.v_scale,
+                                        f8.block_table, f8.seq_lens, causal=Sq > 1,
+                                        return_lse=True)
+    out, lse = pgqa.decode(q.to(cuda_device), d.k, d.v, d.block_table, d.seq_lens,
+                           k_scale=d.k_scale, v_scale=d.v_scale, causal=Sq > 1,
+                           return_lse=True)
     torch.cuda.synchronize()
-    assert_parity(out, ref, what="fp8")
-    assert_lse(lse, ref_lse, "fp8")
+    assert_parity(out, ref, edge=Sq > 1, what=f"fp8 Sq={Sq}")
+    assert_lse(lse, ref_lse, f"fp8 Sq={Sq}")
 
 
 def test_lse_with_appended_tokens(cuda_device):
