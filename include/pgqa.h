@@ -198,29 +198,44 @@ int pgqa_append_kv_fp8(const void* k_new, const void* v_new, void* k_cache, void
 /*
  * Allocation-free variant of pgqa_decode_v1 (no counterpart in the reference).
  *
- * Some callers cannot allocate device memory when they call the decode: code running
- * while a CUDA graph is being captured (cudaMalloc is not allowed there), serving
+ * Some callers cannot allocate device memory when they call the decode: serving
  * engines that reserve nearly all of HBM in their own pool and allow no other
- * allocation on the hot path (cudaMalloc may also synchronise the device), and
- * plugin hosts that hand the operator only its input and output buffers.  This entry
- * point takes the same arguments as pgqa_decode_v1 minus the workspace and allocates
- * nothing: its scratch (split records and arrival counters) lives in a fixed 4 MiB
- * device array inside the library, which every GPU that loads the library holds until
- * the process exits.  Shapes needing more (about 50,000 sequence x KV-head units on a
- * 148-SM B200) are rejected with PGQA_ERR_SCRATCH_LIMIT before anything is launched.
- * The caller still passes q, the pools, seq_lens, block_table and out.
+ * allocation on the hot path (cudaMalloc may also synchronise the device, which stalls
+ * every stream), and plugin hosts that hand the operator only its input and output
+ * buffers and have no workspace to give.  This entry point takes the same arguments as
+ * pgqa_decode_v1 minus the workspace and allocates nothing: its scratch (split records
+ * and arrival counters) lives in a fixed 4 MiB device array inside the library, which
+ * every GPU that loads the library holds until the process exits.  The caller still
+ * passes q, the pools, seq_lens, block_table and out.
  *
- * The first call on a device looks up the array's device address (done once per
- * device, with that device current); make that first call before any stream capture.
- * Each call clears the parts of the array that must start at zero.  All calls share
- * the one array, so calls that overlap on the GPU (different streams, or different
- * host threads) race and give wrong results: order them on one stream.
+ * Limit: after the split records of a 148-SM B200 (2.58 MB) the array holds 50,552
+ * arrival-counter entries, one per (sequence, unit, row group):
+ *     batch_size * num_heads_k * G <= 50,552,
+ *     G = 1 for up to 8 query heads per KV head, else 2 * ceil(ceil(g / 8) / 2)
+ * (g = num_heads / num_heads_k): about 50,500 sequence x KV-head pairs at g <= 8,
+ * 25,200 at g = 16, 12,600 at g = 32, 6,300 at g = 64.  The exact test is
+ * pgqa_make_plan(...).workspace_bytes <= 4 MiB.  Larger shapes are rejected with
+ * PGQA_ERR_SCRATCH_LIMIT before anything is launched.
+ *
+ * The first call on a device looks up the array's device address (once per device,
+ * with that device current) and clears its error word; make that first call before
+ * any stream capture.  Each call clears the arrival counters.  All calls share the one
+ * array, so calls that overlap on the GPU (different streams, or different host
+ * threads) race and give wrong results: order them on one stream.  Device-side errors
+ * (bad page id, length above capacity, expired wait) are kept in the array's error
+ * word until pgqa_noalloc_check_device_error reads them.
  */
 int pgqa_decode_noalloc(const void* q, const void* k_cache, const void* v_cache, void* out,
                         const int32_t* seq_lens, const int32_t* block_table,
                         int64_t batch_size, int64_t num_heads, int64_t num_heads_k,
                         int64_t headdim, int64_t page_size, int64_t num_pages,
                         int64_t bt_stride, int64_t max_seqlen, float scale, void* stream);
+
+/* Synchronous: waits for `stream`, then reads and clears the device-side error word that
+ * pgqa_decode_noalloc calls on the current device share (no counterpart in the
+ * reference).  Returns PGQA_OK (also when no such call has run on this device) or one
+ * of the PGQA_ERR_DEVICE_* codes.  Allocates nothing. */
+int pgqa_noalloc_check_device_error(void* stream);
 
 /* Bytes of workspace pgqa_decode_v1 needs for this shape on the current device
  * (no counterpart in the reference, whose workspace is a hidden static buffer,

@@ -73,6 +73,7 @@ SIGNATURES = {
     "pgqa_last_status": (ctypes.c_int, []),
     "pgqa_status_string": (c_char_p, [ctypes.c_int]),
     "pgqa_check_device_error": (ctypes.c_int, [c_void_p, c_void_p]),
+    "pgqa_noalloc_check_device_error": (ctypes.c_int, [c_void_p]),
     "pgqa_make_plan": (ctypes.c_int, [c_int64] * 5 + [c_int32, c_int32,
                                                       ctypes.POINTER(PgqaPlan)]),
     "pgqa_simulate_partition": (c_int64, [c_void_p, c_int64, c_int64, c_int64,

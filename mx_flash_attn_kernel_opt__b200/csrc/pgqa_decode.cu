@@ -102,7 +102,7 @@ struct DecodeParams {
     int32_t spec_chunks;     // chunks per warp prefetched into L2 before griddepcontrol.wait
     int64_t spec_min_total;  // ... only when the call has at least this many chunks in all
     int32_t debug_spec_skew; // test hook: added to every length the speculative pass reads
-    int32_t debug_stuck;     // test hook: CTA 0 / warp 0 first stage expects 16 bytes too many
+    int32_t debug_stuck;     // test hook: n > 0 makes CTA 0 / warp n-1's first stage expect 16 bytes too many
     uint64_t wait_limit_ns;  // bound on every mbarrier wait
 };
 
@@ -516,7 +516,7 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
                 const int32_t kvh = ikvh;
                 const int32_t z = pid * P + ioff;
                 const uint32_t extra =
-                    (p.debug_stuck && blockIdx.x == 0 && warp == 0 && issued == 0) ? 16u : 0u;
+                    (p.debug_stuck == warp + 1 && blockIdx.x == 0 && issued == 0) ? 16u : 0u;
                 ptx::mbar_arrive_expect_tx(bar, kStage + extra);
                 if (KV8) {
                     ptx::tma_load_3d(dst, &kmap, bar, 0, kvh, z, pol);
@@ -958,6 +958,40 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
                 i += 1;
             }
         }
+
+        if (aborted) {
+            /* A wait expired and the warp stopped early.  It still parks a state for each
+             * unit its slice cuts (the slice's first unit when it starts before the slice
+             * or ends after it; its last unit when it ends after the slice), in the slots
+             * a complete run would have used, with weight zero (lse = -inf, o = 0).  The
+             * CTA then arrives on every arrival counter it owns, the last arriver of each
+             * resets it, and the workspace is left zeroed for the next call even though
+             * this call's output is not valid (the error word says so). */
+            const Cursor u0 = locate(p, pre, ws);
+            const Cursor u1 = locate(p, pre, we - 1);
+            const bool same = (u0.b == u1.b && u0.j == u1.j);
+            have_first = (u0.c != 0) || (same && u1.c != u1.n - 1);
+            have_last = !same && (u1.c != u1.n - 1);
+            first_u = u0;
+            last_u = u1;
+#pragma unroll
+            for (int gr = 0; gr < NG; ++gr) {
+                m2[gr][0] = m2[gr][1] = -INFINITY;
+#pragma unroll
+                for (int mt = 0; mt < 8; ++mt) o[gr][mt][0] = o[gr][mt][1] = o[gr][mt][2] = o[gr][mt][3] = 0.f;
+                if (kEarlyStash && have_first) {
+                    const uint32_t a0 = early_base + (uint32_t)((warp * NG + gr) * sizeof(Stash));
+#pragma unroll
+                    for (int mt = 0; mt < 8; ++mt)
+                        ptx::sts_f4(a0 + (mt * 32 + lane) * 16, make_float4(0.f, 0.f, 0.f, 0.f));
+                    if (gid == 0)
+                        ptx::sts_f2(a0 + offsetof(Stash, lse) + tig * 8, make_float2(-INFINITY, -INFINITY));
+                }
+            }
+#pragma unroll
+            for (int mt = 0; mt < 8; ++mt) fo[mt][0] = fo[mt][1] = fo[mt][2] = fo[mt][3] = 0.f;
+            flse[0] = flse[1] = -INFINITY;
+        }
     }
 
     // Streaming is over: let the next kernel in the stream start launching (it still
@@ -984,8 +1018,8 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
     };
     const uint32_t keys_base = ptx::smem_u32(misc + 32);  // int2 keys[2 W NG]
     {
-        const bool v0 = (warp < wa) && have_first && !aborted;
-        const bool v1 = (warp < wa) && have_last && !aborted;
+        const bool v0 = (warp < wa) && have_first;
+        const bool v1 = (warp < wa) && have_last;
         if (v0 && !kEarlyStash) {
             const uint32_t a0 = stash_addr(2 * warp);
 #pragma unroll
@@ -1579,12 +1613,13 @@ int decode_impl(const void* q, const void* k, const void* v, void* out, const in
     p.cap_tokens = cap;
     p.scale_log2 = scale * 1.4426950408889634f;
     p.min_chunks = plan.min_chunks_per_warp;
-    // Test hooks, read per call: PGQA_DEBUG_STUCK_BARRIER=1 makes one stage barrier wait
-    // for 16 bytes that never arrive (its wait expires -> PGQA_ERR_DEVICE_TIMEOUT);
+    // Test hooks, read per call: PGQA_DEBUG_STUCK_BARRIER=n (n > 0) makes the first stage
+    // barrier of warp n-1 in CTA 0 wait for 16 bytes that never arrive (its wait expires
+    // -> PGQA_ERR_DEVICE_TIMEOUT);
     // PGQA_WAIT_LIMIT_NS shortens the bound on every wait; PGQA_DEBUG_SPEC_SKEW=n adds n
     // to the lengths the speculative pass sees, as if a predecessor had rewritten them
     // (and runs that pass whatever the size of the call).
-    p.debug_stuck = env_int("PGQA_DEBUG_STUCK_BARRIER", 0) != 0;
+    p.debug_stuck = env_int("PGQA_DEBUG_STUCK_BARRIER", 0);
     p.debug_spec_skew = env_int("PGQA_DEBUG_SPEC_SKEW", 0);
     p.spec_chunks = spec_chunks_for(B, plan, cap, kv8);
     // The sweep knob and the test hook run the whole pass whatever the size of the call.
@@ -1860,6 +1895,27 @@ extern "C" const char* pgqa_status_string(int status) {
     }
 }
 
+namespace {
+/* Waits for `s`, reads the 4-byte device error word at `word_ptr`, clears it when it is
+ * set, and maps its bits to a status. */
+int read_error_word(void* word_ptr, cudaStream_t s) {
+    int32_t word = 0;
+    if (cudaMemcpyAsync(&word, word_ptr, 4, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+        cudaStreamSynchronize(s) != cudaSuccess) {
+        cudaGetLastError();
+        return PGQA_ERR_CUDA;
+    }
+    if (word != 0) {
+        cudaMemsetAsync(word_ptr, 0, 4, s);
+        cudaStreamSynchronize(s);
+    }
+    if (word & kErrTimeout) return PGQA_ERR_DEVICE_TIMEOUT;
+    if (word & kErrBadPage) return PGQA_ERR_DEVICE_BAD_PAGE;
+    if (word & kErrBadSeqlen) return PGQA_ERR_DEVICE_BAD_SEQLEN;
+    return PGQA_OK;
+}
+}  // namespace
+
 extern "C" int pgqa_check_device_error(void* workspace, void* stream) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) {
@@ -1871,21 +1927,7 @@ extern "C" int pgqa_check_device_error(void* workspace, void* stream) {
         if (dev < 0 || dev >= kMaxDevices || g_ws[dev].ptr == nullptr) return PGQA_OK;
         workspace = g_ws[dev].ptr;
     }
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    int32_t word = 0;
-    if (cudaMemcpyAsync(&word, workspace, 4, cudaMemcpyDeviceToHost, s) != cudaSuccess ||
-        cudaStreamSynchronize(s) != cudaSuccess) {
-        cudaGetLastError();
-        return PGQA_ERR_CUDA;
-    }
-    if (word != 0) {
-        cudaMemsetAsync(workspace, 0, 4, s);
-        cudaStreamSynchronize(s);
-    }
-    if (word & kErrTimeout) return PGQA_ERR_DEVICE_TIMEOUT;
-    if (word & kErrBadPage) return PGQA_ERR_DEVICE_BAD_PAGE;
-    if (word & kErrBadSeqlen) return PGQA_ERR_DEVICE_BAD_SEQLEN;
-    return PGQA_OK;
+    return read_error_word(workspace, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int pgqa_make_plan(int64_t batch_size, int64_t num_heads, int64_t num_heads_k,
@@ -1944,9 +1986,10 @@ extern "C" const char* pgqa_version(void) { return "pgqa-b200 0.1 (sm_100a)"; }
 
 /* Scratch for pgqa_decode_noalloc: the same layout pgqa_decode_v1 expects of a caller's
  * workspace (error word, split records, arrival counters), held in a fixed array that
- * every GPU loading this library keeps until the process exits.  4 MiB covers the
- * records of a 148-SM B200 (2.6 MB, sized for two row groups per unit) plus arrival
- * counters for about 50,000 (sequence, KV head, row group) units. */
+ * every GPU loading this library keeps until the process exits.  On a 148-SM B200 the
+ * records take 2.58 MB (sized for two row groups per unit), leaving 50,552 arrival-
+ * counter entries of 32 bytes, one per (sequence, unit, row group): B * Hkv at up to 8
+ * query heads per KV head, B * Hkv * 2 * ceil(ceil(g/8)/2) beyond. */
 constexpr size_t kNoAllocScratchBytes = (size_t)4 << 20;
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
 
@@ -1961,8 +2004,9 @@ std::mutex g_noalloc_mu;
 
 /* Host code may not use g_noalloc_scratch itself (that name is a host-side stand-in,
  * not a device address): resolve the device address once per device, with that device
- * current. */
-int noalloc_scratch(int dev, void** out) {
+ * current.  *fresh is set on the call that did the look-up. */
+int noalloc_scratch(int dev, void** out, bool* fresh) {
+    *fresh = false;
     if (dev < 0 || dev >= pgqa::kMaxDevices) return PGQA_ERR_NO_DEVICE;
     std::lock_guard<std::mutex> lk(g_noalloc_mu);
     NoAllocScratch& s = g_noalloc[dev];
@@ -1975,6 +2019,7 @@ int noalloc_scratch(int dev, void** out) {
         } else {
             s.ptr = p;
             s.status = PGQA_OK;
+            *fresh = true;
         }
         s.init = true;
     }
@@ -2004,15 +2049,18 @@ extern "C" int pgqa_decode_noalloc(const void* q, const void* k_cache, const voi
     if ((size_t)plan.workspace_bytes > kNoAllocScratchBytes)
         return set_status(PGQA_ERR_SCRATCH_LIMIT);
     void* scratch = nullptr;
-    st = noalloc_scratch(dev, &scratch);
+    bool fresh = false;
+    st = noalloc_scratch(dev, &scratch, &fresh);
     if (st != PGQA_OK) return set_status(st);
-    // The array keeps the previous call's contents: the error word and the arrival
-    // counters must start at zero (a failed call may have left counters behind).
+    // The array keeps the previous call's contents.  The arrival counters must start at
+    // zero for every call (the kernel leaves them zeroed, this is a second guard).  The
+    // error word is cleared once, at set-up, and otherwise only by
+    // pgqa_noalloc_check_device_error: an error stays readable until the caller reads it.
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     uint8_t* base = static_cast<uint8_t*>(scratch);
     const size_t counters_off = 256 + records_bytes(plan.grid_ctas);
     const size_t counters_len = (size_t)plan.workspace_bytes - counters_off;
-    if (cudaMemsetAsync(base, 0, 256, s) != cudaSuccess ||
+    if ((fresh && cudaMemsetAsync(base, 0, 256, s) != cudaSuccess) ||
         cudaMemsetAsync(base + counters_off, 0, counters_len, s) != cudaSuccess) {
         cudaGetLastError();
         return set_status(PGQA_ERR_CUDA);
@@ -2023,3 +2071,20 @@ extern "C" int pgqa_decode_noalloc(const void* q, const void* k_cache, const voi
                                   s));
 }
 
+
+extern "C" int pgqa_noalloc_check_device_error(void* stream) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) {
+        cudaGetLastError();
+        return PGQA_ERR_NO_DEVICE;
+    }
+    if (dev < 0 || dev >= pgqa::kMaxDevices) return PGQA_ERR_NO_DEVICE;
+    void* scratch = nullptr;
+    {
+        std::lock_guard<std::mutex> lk(g_noalloc_mu);
+        const NoAllocScratch& sc = g_noalloc[dev];
+        if (!sc.init || sc.status != PGQA_OK) return PGQA_OK;  // no call has run here
+        scratch = sc.ptr;
+    }
+    return read_error_word(scratch, static_cast<cudaStream_t>(stream));
+}

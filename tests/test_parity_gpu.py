@@ -7,6 +7,7 @@ Acceptance, per case:
   * block-table indexing bit-exact: pools poisoned with NaN in every slot a correct
     kernel must not read still give finite, matching outputs.
 """
+import ctypes
 import math
 import os
 import subprocess
@@ -288,7 +289,8 @@ def test_seq_len_above_capacity_is_reported(cuda_device):
 
 def test_expired_wait_reports_timeout_and_context_survives(cuda_device, monkeypatch):
     """One stage barrier waits for 16 bytes nothing sends: its bounded wait expires, the
-    kernel records PGQA_ERR_DEVICE_TIMEOUT and returns; the context stays usable."""
+    kernel records PGQA_ERR_DEVICE_TIMEOUT and returns; the context stays usable and the
+    workspace is left ready for the next call (no manual reset)."""
     inp = inputs.custom_case(2, 32, 8, 16, [300, 200], seed=8)
     d = inp.to(cuda_device)
     ws = _fresh_ws(inp, cuda_device)
@@ -300,11 +302,74 @@ def test_expired_wait_reports_timeout_and_context_survives(cuda_device, monkeypa
     assert e.value.status == 8
     monkeypatch.delenv("PGQA_DEBUG_STUCK_BARRIER")
     monkeypatch.delenv("PGQA_WAIT_LIMIT_NS")
-    ws.zero_()  # a call that failed may leave arrival counters behind
     out = pgqa.decode(d.q, d.k, d.v, d.block_table, d.seq_lens, workspace=ws)
     pgqa.check_device_error(ws)
     ref = paged_decode_ref(inp.q, inp.k, inp.v, inp.block_table, inp.seq_lens)
     assert_parity(out, ref, what="after timeout")
+
+
+def _slice_begin(i, n, total):
+    return i * total // n
+
+
+def _sole_holder_case():
+    """B=1, Hq=32, Hkv=8, L=240: 8 units of 15 chunks, 120 chunks over 7 CTAs of 8 warps
+    (2 chunks per warp at least).  CTA 0 owns chunks [0, 17); its warp 7 owns [14, 17),
+    the last chunk of unit 0 and the first two of unit 1, which continues in CTA 1.  So
+    warp 7 is the only holder of unit 1 in CTA 0: if it stops, CTA 0 must still arrive
+    on unit 1's counters, or the next call would merge unit 1 one CTA early."""
+    inp = inputs.custom_case(1, 32, 8, 16, [240], seed=31)
+    T, n_cta, W = 15 * 8, 120 // 16, 8
+    cta0_end = _slice_begin(1, n_cta, T)
+    w7 = (_slice_begin(7, W, cta0_end), _slice_begin(8, W, cta0_end))
+    assert (n_cta, cta0_end, w7) == (7, 17, (14, 17))
+    return inp
+
+
+@pytest.mark.parametrize("path", ["caller_workspace", "run_kernel"])
+def test_expired_wait_in_the_only_holder_of_a_cut_unit_leaves_counters_clean(
+        path, cuda_device, monkeypatch):
+    """The stalled warp parks a zero-weight state for each unit its slice cuts, so every
+    arrival counter completes and is reset by its last arriver; the next call on the same
+    workspace (the caller's, or run_kernel's library workspace, which the caller cannot
+    reset) is correct without any manual reset."""
+    inp = _sole_holder_case()
+    d = inp.to(cuda_device)
+    ws = _fresh_ws(inp, cuda_device) if path == "caller_workspace" else None
+
+    def call():
+        if ws is not None:
+            return pgqa.decode(d.q, d.k, d.v, d.block_table, d.seq_lens, workspace=ws)
+        out = torch.zeros_like(d.q)
+        B, Hq, D = d.q.shape
+        L = _lib.lib()
+        with torch.cuda.device(cuda_device):
+            L.run_kernel(ctypes.c_void_p(d.q.data_ptr()), ctypes.c_void_p(d.k.data_ptr()),
+                         ctypes.c_void_p(d.v.data_ptr()), ctypes.c_void_p(out.data_ptr()),
+                         ctypes.c_void_p(d.seq_lens.data_ptr()),
+                         ctypes.c_void_p(d.block_table.data_ptr()), B, inp.seqlen_k, 1, Hq,
+                         inp.num_heads_k, D, inp.page_size, inp.num_pages, 0)
+        assert L.pgqa_last_status() == 0
+        return out
+
+    if ws is None:
+        call()  # the library workspace exists (allocated, zeroed) before the failing call
+        torch.cuda.synchronize()
+        pgqa.check_device_error()
+    monkeypatch.setenv("PGQA_DEBUG_STUCK_BARRIER", "8")  # warp 7 of CTA 0
+    monkeypatch.setenv("PGQA_WAIT_LIMIT_NS", "20000000")
+    call()
+    with pytest.raises(pgqa.PgqaError) as e:
+        pgqa.check_device_error(ws)
+    assert e.value.status == 8
+    monkeypatch.delenv("PGQA_DEBUG_STUCK_BARRIER")
+    monkeypatch.delenv("PGQA_WAIT_LIMIT_NS")
+    ref = paged_decode_ref(inp.q, inp.k, inp.v, inp.block_table, inp.seq_lens)
+    for k in range(2):
+        out = call()
+        torch.cuda.synchronize()
+        pgqa.check_device_error(ws)
+        assert_parity(out, ref, what=f"call {k} after timeout ({path})")
 
 
 def test_library_workspace_allocation_failure_is_reported(cuda_device):
