@@ -59,6 +59,7 @@
 #include "pgqa_append.h"
 #include "pgqa_partition.h"
 #include "pgqa_ptx.cuh"
+#include "pgqa_tc.h"
 
 namespace pgqa {
 
@@ -1196,10 +1197,10 @@ int env_int(const char* name, int dflt) {
     return atoi(v);
 }
 
-/* Sweep knobs (unset in normal use): PGQA_WARPS, PGQA_STAGES, PGQA_MIN_CHUNKS, PGQA_GRID,
- * PGQA_NO_PDL (plain launch instead of a programmatic dependent launch), PGQA_NG (1: one
- * row group per unit even where two would share the K/V tiles), PGQA_SPEC (chunks per
- * warp prefetched into L2 before griddepcontrol.wait; 0: none). */
+/* Sweep knobs (unset in normal use, read once): PGQA_WARPS, PGQA_STAGES, PGQA_MIN_CHUNKS,
+ * PGQA_GRID, PGQA_NO_PDL (plain launch instead of a programmatic dependent launch),
+ * PGQA_NG (1: one row group per unit even where two would share the K/V tiles),
+ * PGQA_SPEC (chunks per warp prefetched into L2 before griddepcontrol.wait; 0: none). */
 struct Knobs {
     int warps, stages, min_chunks, grid, no_pdl, ng, spec;
 };
@@ -1230,6 +1231,17 @@ int spec_chunks_for(int64_t B, const pgqa_plan& plan, int64_t cap_tokens, bool k
     const int64_t chunks = B * plan.units_per_seq * ((cap_tokens + kChunkTokens - 1) / kChunkTokens);
     if (chunks < spec_min_total_for(plan)) return 0;
     return kv8 ? kDefaultSpecChunksKv8 : kDefaultSpecChunks;
+}
+
+// The tensor-core (tcgen05) variant, for KV heads with at most kTcMaxRows query rows.
+// PGQA_TC (read per call): 1 runs it wherever it applies (one-token bf16 decodes
+// included), 0 or unset keeps the mma.sync kernel, which measures faster today on every
+// named configuration.
+constexpr int kTcMinChunks = 8;  // at least one 128-token tile per active CTA
+
+bool use_tc(int64_t rows, size_t smem, int smem_optin) {
+    if (rows > kTcMaxRows || smem > (size_t)smem_optin) return false;
+    return env_int("PGQA_TC", 0) == 1;
 }
 
 constexpr int kDefaultWarps = 8;
@@ -1650,6 +1662,43 @@ int decode_impl(const void* q, const void* k, const void* v, void* out, const in
         a.cap_tokens = cap;
         a.row_pieces_log2 = kv8 ? 3 : 4;
         if (launch_append(a, di.sms, stream) != 0) return PGQA_ERR_CUDA;
+    }
+    const size_t tc_smem = tc_smem_bytes(kv8, (int)(g * Sq), B);
+    if (use_tc(g * Sq, tc_smem, di.smem_optin)) {
+        TcParams t;
+        t.q = p.q;
+        t.out = p.out;
+        t.lse_out = p.lse_out;
+        t.seq_lens = p.seq_lens;
+        t.block_table = p.block_table;
+        t.rec_o = p.rec_o;
+        t.rec_lse = p.rec_lse;
+        t.counters = p.counters;
+        t.err = p.err;
+        t.B = p.B;
+        t.Hq = p.Hq;
+        t.Hkv = p.Hkv;
+        t.g = p.g;
+        t.Sq = p.Sq;
+        t.rows = p.rows;
+        t.causal = p.causal;
+        t.len_add = p.len_add;
+        t.k_scale = p.k_scale;
+        t.v_scale = p.v_scale;
+        t.page_size = p.page_size;
+        t.bt_stride = p.bt_stride;
+        t.num_pages = p.num_pages;
+        t.cap_tokens = p.cap_tokens;
+        t.scale_log2 = p.scale_log2;
+        t.min_chunks = knobs().min_chunks > 0 ? knobs().min_chunks : kTcMinChunks;
+        t.debug_stuck = p.debug_stuck;
+        t.wait_limit_ns = p.wait_limit_ns;
+        if (launch_tc(km, vm, t, kv8, plan.grid_ctas, tc_smem, knobs().no_pdl == 0, stream) !=
+            cudaSuccess) {
+            cudaGetLastError();
+            return PGQA_ERR_CUDA;
+        }
+        return PGQA_OK;
     }
     return launch(plan, km, vm, p, kv8, stream);
 }

@@ -19,3 +19,11 @@ def cuda_device():
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
     return torch.device("cuda", 0)
+
+
+@pytest.fixture(params=["mma", "tc"])
+def both_kernels(request, monkeypatch):
+    """Runs a test on the mma.sync kernel and on the tcgen05 variant (PGQA_TC, read by the
+    library on every call; shapes the variant does not cover stay on mma.sync)."""
+    monkeypatch.setenv("PGQA_TC", "1" if request.param == "tc" else "0")
+    return request.param

@@ -14,7 +14,7 @@ from mx_flash_attn_kernel_opt__b200 import inputs
 from oracle import append_kv_ref, paged_decode_fp8_ref
 from tests.test_parity_gpu import assert_parity
 
-pytestmark = pytest.mark.gpu
+pytestmark = [pytest.mark.gpu, pytest.mark.usefixtures("both_kernels")]
 
 
 def run_fp8(inp, dev, q=None, **kw):

@@ -11,7 +11,7 @@ from mx_flash_attn_kernel_opt__b200 import inputs
 from oracle import append_kv_ref, paged_decode_fp8_ref, paged_decode_ref
 from tests.test_parity_gpu import assert_parity
 
-pytestmark = pytest.mark.gpu
+pytestmark = [pytest.mark.gpu, pytest.mark.usefixtures("both_kernels")]
 
 # fp32 log-sum-exp: the kernel uses ex2.approx / lg2.approx on the same bf16 inputs
 LSE_ATOL = LSE_RTOL = 1e-3

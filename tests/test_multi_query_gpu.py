@@ -15,7 +15,7 @@ from mx_flash_attn_kernel_opt__b200 import inputs
 from oracle import paged_decode_ref
 from tests.test_parity_gpu import assert_parity
 
-pytestmark = pytest.mark.gpu
+pytestmark = [pytest.mark.gpu, pytest.mark.usefixtures("both_kernels")]
 
 
 def multi_query_case(B, Sq, Hq, Hkv, P, lens, seed, table="permuted"):
