@@ -1234,14 +1234,22 @@ int spec_chunks_for(int64_t B, const pgqa_plan& plan, int64_t cap_tokens, bool k
 }
 
 // The tensor-core (tcgen05) variant, for KV heads with at most kTcMaxRows query rows.
-// PGQA_TC (read per call): 1 runs it wherever it applies (one-token bf16 decodes
-// included), 0 or unset keeps the mma.sync kernel, which measures faster today on every
-// named configuration.
-constexpr int kTcMinChunks = 8;  // at least one 128-token tile per active CTA
+// Measured on B200 against the mma.sync kernel, it is faster for bf16 pools with more than
+// 16 query rows per KV head (several query tokens) over long sequences -- four tokens:
+// 0.86x the time on c2, 0.76x on c4, 0.62x on c5 -- and slower for short sequences (1.27x
+// on c3, where every unit costs it a fixed epilogue and a partial tile), for one query
+// token (1.21x on c2) and for e4m3 pools (1.74x on c2: the V tiles must be converted to
+// f16 on the way).  The table capacity stands in for the lengths, which only the device
+// reads.  PGQA_TC (read per call) overrides: 1 runs the variant wherever it applies, 0
+// never.
+constexpr int kTcMinChunks = 8;           // at least one 128-token tile per active CTA
+constexpr int64_t kTcMinCapacity = 8192;  // tokens of table capacity for the default choice
 
-bool use_tc(int64_t rows, size_t smem, int smem_optin) {
+bool use_tc(int64_t rows, int64_t Sq, bool kv8, int64_t cap_tokens, size_t smem, int smem_optin) {
     if (rows > kTcMaxRows || smem > (size_t)smem_optin) return false;
-    return env_int("PGQA_TC", 0) == 1;
+    const int forced = env_int("PGQA_TC", -1);
+    if (forced >= 0) return forced == 1;
+    return !kv8 && Sq > 1 && rows > 16 && cap_tokens >= kTcMinCapacity;
 }
 
 constexpr int kDefaultWarps = 8;
@@ -1664,7 +1672,7 @@ int decode_impl(const void* q, const void* k, const void* v, void* out, const in
         if (launch_append(a, di.sms, stream) != 0) return PGQA_ERR_CUDA;
     }
     const size_t tc_smem = tc_smem_bytes(kv8, (int)(g * Sq), B);
-    if (use_tc(g * Sq, tc_smem, di.smem_optin)) {
+    if (use_tc(g * Sq, Sq, kv8, cap, tc_smem, di.smem_optin)) {
         TcParams t;
         t.q = p.q;
         t.out = p.out;

@@ -246,20 +246,6 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
     return d;
 }
 
-/* Four e4m3 bytes -> two f16x2 with integer operations (no conversion unit): the bit
- * pattern (sign to bit 15, exponent and mantissa to bits 7..13) is exactly the f16 value
- * times 2^-8 (subnormals included), and one f16x2 multiply by 2^8 restores it.  The e4m3
- * NaN pattern is not preserved (it becomes 480). */
-__device__ __forceinline__ void e4m3x4_to_f16_alu(uint32_t w, uint32_t& lo, uint32_t& hi) {
-    const uint32_t a = prmt(w, 0u, 0x1404u);  // 16-bit lanes b0 << 8, b1 << 8
-    const uint32_t b = prmt(w, 0u, 0x3424u);  // 16-bit lanes b2 << 8, b3 << 8
-    const uint32_t la = ((a >> 1) & 0x3F803F80u) | (a & 0x80008000u);
-    const uint32_t lb = ((b >> 1) & 0x3F803F80u) | (b & 0x80008000u);
-    const uint32_t k256 = 0x5C005C00u;        // f16x2 (256, 256)
-    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(lo) : "r"(la), "r"(k256));
-    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(hi) : "r"(lb), "r"(k256));
-}
-
 __device__ __forceinline__ uint32_t movmatrix_t(uint32_t a) {
     uint32_t d;
     asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(a));

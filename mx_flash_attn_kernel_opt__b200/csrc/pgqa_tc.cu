@@ -180,10 +180,17 @@ struct Smem {
     static constexpr int kBars = 2 * SK + 2 * SV + 18;
     static constexpr int kMiscOff = (kBarOff + kBars * 8 + 15) / 16 * 16;
     // misc: [0] TMEM base, [4] abort flag, [16..48) warp sums, [48..80) exchange words
-    // [2][4], then red[2][NP][4] f32, mul[2][NP] f32, then the prefix table
+    // [2][4], then red[2][NP][4] f32, mul[2][NP] f32, row offsets and causal masks [NP] each,
+    // then the prefix table
     static constexpr int kRedOff = kMiscOff + 80;
     static constexpr int kMulOff = kRedOff + 2 * NP * 4 * 4;
-    static constexpr int kPreOff = kMulOff + 2 * NP * 4;
+    static constexpr int kRowOff = kMulOff + 2 * NP * 4;   // [NP] row offsets in q / out
+    static constexpr int kVisOff = kRowOff + NP * 4;       // [NP] causal visibility masks
+    static constexpr int kLPartOff = kVisOff + NP * 4;      // [2][NP][4] per-warp row sums of a piece
+    static constexpr int kMRefOff = kLPartOff + 2 * NP * 16; // [2][NP] reference maxima of a piece
+    static constexpr int kStgOff = (kMRefOff + 2 * NP * 4 + 15) / 16 * 16;  // epilogue staging
+    static constexpr int kStg = NP * kHeadDim * 4;                           // (8 KB at 16 rows or 32)
+    static constexpr int kPreOff = kStgOff + (NP == 16 ? kStg : kStg / 2);
     static size_t bytes(int64_t B) { return 1024 + kPreOff + (size_t)(B + 1) * 4 + 16; }
 };
 
@@ -211,6 +218,11 @@ pgqa_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
     volatile int32_t* xword = reinterpret_cast<volatile int32_t*>(smem + L::kMiscOff + 48);  // [2][4]
     float* red = reinterpret_cast<float*>(smem + L::kRedOff);    // [2][NP][4]
     float* mulv = reinterpret_cast<float*>(smem + L::kMulOff);   // [2][NP]
+    int32_t* roff = reinterpret_cast<int32_t*>(smem + L::kRowOff);
+    uint32_t* vism = reinterpret_cast<uint32_t*>(smem + L::kVisOff);
+    float* lpart = reinterpret_cast<float*>(smem + L::kLPartOff);
+    float* mrefs = reinterpret_cast<float*>(smem + L::kMRefOff);
+    uint8_t* stg = smem + L::kStgOff;  // normalised rows of a piece, [NP][128] (fp32 at 16 rows, bf16 else)
     uint32_t* pre = reinterpret_cast<uint32_t*>(smem + L::kPreOff);
 
     // barrier addresses
@@ -346,6 +358,17 @@ pgqa_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
     if (warp == 3) {
         ptx::tmem_alloc(ptx::smem_u32(tmem_slot), kTmemCols);
         ptx::tmem_relinquish();
+    }
+    if (tid < NP) {
+        // row r of a KV head = (head r / Sq, token r % Sq): its offset in q / out relative
+        // to (sequence b, KV head kvh), and the rows a key at distance k past
+        // L - Sq + 1 stays visible to under the causal mask (bit r set: r % Sq > k)
+        const int h = MQ ? tid / p.Sq : tid, i = MQ ? tid - (tid / p.Sq) * p.Sq : 0;
+        roff[tid] = (i * p.Hq + h) * kHeadDim;
+        uint32_t m = 0;
+        for (int r = 0; r < NP; ++r)
+            if (MQ && (r - (r / p.Sq) * p.Sq) > tid) m |= 1u << r;
+        vism[tid] = m;
     }
     ptx::tc_fence_before();
     __syncthreads();
@@ -629,9 +652,10 @@ pgqa_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
             if (NP == 32) ptx::tc_st16((col + 16) | lane_off, *reinterpret_cast<const float(*)[16]>(&v[16]));
         };
 
-        float m_ref[NP], l_part[NP], mul[NP];
-        int32_t lim[MQ ? NP : 1];
+        float m_ref[NP], l_part[NP];
+        float mul[KV8 ? NP : 1];  // bf16: one score multiplier for every row
         float vsc = 1.f;
+        int32_t causal_base = 0;  // keys past L - Sq + 1 are seen by some rows only
         int32_t piece_c0 = 0;
         bool done_cut_first = false, done_cut_last = false;
         // cut units of this slice: the one holding chunk cs (if it starts before cs) and
@@ -655,27 +679,22 @@ pgqa_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
 
         // record, arrival and (for the last arriver) merge of a unit cut by slice bounds
         // (`arrived` is set once this CTA's arrival on the counter is certain)
-        auto finish_cut = [&](int32_t b, int32_t kvh, int32_t n, const float (&o)[NP],
-                              const float (&inv)[NP], const float (&lse2)[NP], bool live,
-                              bool& arrived) -> bool {
+        // the normalised row and its log2-sum-exp from O, the row sum l and the reference
+        auto norm_of = [&](float o, float l, float vs) { return (!MQ || l > 0.f) ? o * __fdividef(vs, l) : 0.f; };
+        auto lse2_of = [&](float m, float l) { return (!MQ || l > 0.f) ? m + ptx::lg2(l) : -INFINITY; };
+        // record slot of this CTA for the unit (b, kvh) of n chunks
+        auto slot_of = [&](int32_t b, int32_t kvh, int32_t n) {
+            return record_slot(blockIdx.x, cs, (int64_t)pre[b] * p.Hkv + (int64_t)kvh * n);
+        };
+        // record row r (thread st writes dimension st)
+        auto put_rec = [&](int64_t slot, int r, float v) {
+            if (NP == 16) reinterpret_cast<float*>(p.rec_o)[(slot * NP + r) * kHeadDim + st] = v;
+            else reinterpret_cast<__nv_bfloat16*>(p.rec_o)[(slot * NP + r) * kHeadDim + st] = __float2bfloat16_rn(v);
+        };
+        // arrival on the counter of a cut unit whose record this CTA has written, and the
+        // merge of all its records by the last CTA to arrive
+        auto arrive_merge = [&](int32_t b, int32_t kvh, int32_t n, bool live, bool& arrived) -> bool {
             const int64_t ubeg = (int64_t)pre[b] * p.Hkv + (int64_t)kvh * n;
-            const int64_t slot = record_slot(blockIdx.x, cs, ubeg);
-            if (NP == 16) {
-                float* ro = reinterpret_cast<float*>(p.rec_o) + slot * NP * kHeadDim;
-#pragma unroll
-                for (int r = 0; r < NP; ++r) ro[r * kHeadDim + st] = o[r] * inv[r];
-            } else {
-                __nv_bfloat16* ro = reinterpret_cast<__nv_bfloat16*>(p.rec_o) + slot * NP * kHeadDim;
-#pragma unroll
-                for (int r = 0; r < NP; ++r) ro[r * kHeadDim + st] = __float2bfloat16_rn(o[r] * inv[r]);
-            }
-            if (st < NP) {
-                float v = lse2[0];
-#pragma unroll
-                for (int r = 1; r < NP; ++r) v = (st == r) ? lse2[r] : v;
-                p.rec_lse[slot * NP + st] = v;
-            }
-            ptx::fence_acq_rel_gpu();
             const int64_t c_first = slice_owner(ubeg, nct, T);
             const int64_t c_last = slice_owner(ubeg + n - 1, nct, T);
             int32_t* cnt = p.counters + (int64_t)b * p.Hkv + kvh;
@@ -691,71 +710,178 @@ pgqa_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
             if (!xsync()) return false;
             arrived = true;  // thread 0 arrives now, whatever happens next
             if (st == 0) {
+                // releases the record stores of all 128 threads, ordered before this
+                // thread by the exchange barrier (cumulative release)
+                ptx::fence_acq_rel_gpu();
                 const int32_t prev = ptx::atom_add_acq_rel_gpu(cnt, 1);
                 const int last = prev == (int32_t)(c_last - c_first);
-                if (last) *cnt = 0;
+                if (last) {
+                    *cnt = 0;
+                    ptx::fence_acq_rel_gpu();  // the other CTAs' records, for every thread here
+                }
                 xword[(xg_n & 1) * 4] = last;
             }
             if (!xsync()) return false;
             if (!xword[((xg_n - 1) & 1) * 4]) return true;
-            ptx::fence_acq_rel_gpu();
-            // merge the unit's records, first the maxima, then the weighted sums
+            /* Merge the unit's records.  Thread st owns dims [8 dc, 8 dc + 8) of rows
+             * [kR rg, kR rg + kR) (dc = st % 16, rg = st / 16), so every load is a 16-byte
+             * vector; records are read kB at a time, all loads of a batch in flight
+             * together, with the running maxima raised once per batch. */
+            constexpr int kR = NP / 8;  // rows per thread
+            constexpr int kB = 4;       // records per batch
+            const int dc = st & 15, rg = st >> 4;
             const int nrec = (int)(c_last - c_first + 1);
             const int64_t slot0 = record_slot(c_first, slice_begin(c_first, nct, T), ubeg);
-            float M[NP];
+            float mx[kR], den[kR], acc[kR][8];
 #pragma unroll
-            for (int r = 0; r < NP; ++r) M[r] = -INFINITY;
-            for (int k = 0; k < nrec; ++k) {
-                const int64_t sl = (k == 0) ? slot0 : 2 * (c_first + k);
-                const float4* l4 = reinterpret_cast<const float4*>(p.rec_lse + sl * NP);
+            for (int r = 0; r < kR; ++r) {
+                mx[r] = -INFINITY;
+                den[r] = 0.f;
 #pragma unroll
-                for (int r4 = 0; r4 < NP / 4; ++r4) {
-                    const float4 v = __ldcg(l4 + r4);
-                    M[4 * r4] = fmaxf(M[4 * r4], v.x);
-                    M[4 * r4 + 1] = fmaxf(M[4 * r4 + 1], v.y);
-                    M[4 * r4 + 2] = fmaxf(M[4 * r4 + 2], v.z);
-                    M[4 * r4 + 3] = fmaxf(M[4 * r4 + 3], v.w);
+                for (int e = 0; e < 8; ++e) acc[r][e] = 0.f;
+            }
+            for (int k0 = 0; k0 < nrec; k0 += kB) {
+                float lv[kB][kR];
+                uint4 ov[kB][kR][NP == 16 ? 2 : 1];
+#pragma unroll
+                for (int u = 0; u < kB; ++u) {
+                    const bool in = k0 + u < nrec;
+                    const int64_t sl = (k0 + u == 0) ? slot0 : 2 * (c_first + k0 + u);
+#pragma unroll
+                    for (int r = 0; r < kR; ++r) {
+                        const int row = rg * kR + r;
+                        lv[u][r] = in ? __ldcg(p.rec_lse + sl * NP + row) : -INFINITY;
+                        if (NP == 16) {
+                            const uint4* src = reinterpret_cast<const uint4*>(
+                                reinterpret_cast<const float*>(p.rec_o) + (sl * NP + row) * kHeadDim + dc * 8);
+                            ov[u][r][0] = in ? __ldcg(src) : make_uint4(0, 0, 0, 0);
+                            ov[u][r][NP == 16 ? 1 : 0] = in ? __ldcg(src + 1) : make_uint4(0, 0, 0, 0);
+                        } else {
+                            const uint4* src = reinterpret_cast<const uint4*>(
+                                reinterpret_cast<const __nv_bfloat16*>(p.rec_o) + (sl * NP + row) * kHeadDim + dc * 8);
+                            ov[u][r][0] = in ? __ldcg(src) : make_uint4(0, 0, 0, 0);
+                        }
+                    }
                 }
-            }
-            float acc[NP], den[NP];
 #pragma unroll
-            for (int r = 0; r < NP; ++r) {
-                acc[r] = den[r] = 0.f;
-                if (MQ && M[r] == -INFINITY) M[r] = 0.f;  // a row that sees no key keeps weight 0
-            }
-            for (int k = 0; k < nrec; ++k) {
-                const int64_t sl = (k == 0) ? slot0 : 2 * (c_first + k);
-                const float4* l4 = reinterpret_cast<const float4*>(p.rec_lse + sl * NP);
+                for (int r = 0; r < kR; ++r) {
+                    float bm = lv[0][r];
 #pragma unroll
-                for (int r4 = 0; r4 < NP / 4; ++r4) {
-                    const float4 v = __ldcg(l4 + r4);
-                    const float lv[4] = {v.x, v.y, v.z, v.w};
+                    for (int u = 1; u < kB; ++u) bm = fmaxf(bm, lv[u][r]);
+                    if (bm > mx[r]) {  // raise the running maximum, rescaling what was summed
+                        const float sc = (mx[r] == -INFINITY) ? 0.f : ptx::ex2(mx[r] - bm);
+                        den[r] *= sc;
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const int r = 4 * r4 + e;
-                        const float wgt = ptx::ex2(lv[e] - M[r]);
-                        float ov;
-                        if (NP == 16)
-                            ov = __ldcg(reinterpret_cast<const float*>(p.rec_o) + (sl * NP + r) * kHeadDim + st);
-                        else
-                            ov = __bfloat162float(__ldcg(reinterpret_cast<const __nv_bfloat16*>(p.rec_o) +
-                                                         (sl * NP + r) * kHeadDim + st));
-                        acc[r] = fmaf(wgt, ov, acc[r]);
+                        for (int e = 0; e < 8; ++e) acc[r][e] *= sc;
+                        mx[r] = bm;
+                    }
+                    const float base = (MQ && mx[r] == -INFINITY) ? 0.f : mx[r];  // no key: weight 0
+#pragma unroll
+                    for (int u = 0; u < kB; ++u) {
+                        const float wgt = ptx::ex2(lv[u][r] - base);
                         den[r] += wgt;
+                        float f[8];
+                        if (NP == 16) {
+                            const uint4 a = ov[u][r][0], c = ov[u][r][NP == 16 ? 1 : 0];
+                            f[0] = __uint_as_float(a.x); f[1] = __uint_as_float(a.y);
+                            f[2] = __uint_as_float(a.z); f[3] = __uint_as_float(a.w);
+                            f[4] = __uint_as_float(c.x); f[5] = __uint_as_float(c.y);
+                            f[6] = __uint_as_float(c.z); f[7] = __uint_as_float(c.w);
+                        } else {
+                            const uint4 a = ov[u][r][0];
+                            const uint32_t wv[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                f[2 * e] = __uint_as_float(wv[e] << 16);
+                                f[2 * e + 1] = __uint_as_float(wv[e] & 0xffff0000u);
+                            }
+                        }
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) acc[r][e] = fmaf(wgt, f[e], acc[r][e]);
                     }
                 }
             }
 #pragma unroll
-            for (int r = 0; r < NP; ++r) {
-                if (r < p.rows) {
-                    const float v = (!MQ || den[r] > 0.f) ? acc[r] / den[r] : 0.f;
-                    p.out[row_offset<MQ>(p, b, kvh, r) + st] = __float2bfloat16_rn(v);
-                    if (LSE && st == 0)
-                        p.lse_out[lse_index<MQ>(p, b, kvh, r)] =
-                            (den[r] > 0.f ? M[r] + ptx::lg2(den[r]) : -INFINITY) * 0.6931471805599453f;
+            for (int r = 0; r < kR; ++r) {
+                const int row = rg * kR + r;
+                if (row < p.rows) {
+                    const float inv = (!MQ || den[r] > 0.f) ? __fdividef(1.f, den[r]) : 0.f;
+                    uint4 o8;
+                    o8.x = ptx::pack_bf16x2(acc[r][0] * inv, acc[r][1] * inv);
+                    o8.y = ptx::pack_bf16x2(acc[r][2] * inv, acc[r][3] * inv);
+                    o8.z = ptx::pack_bf16x2(acc[r][4] * inv, acc[r][5] * inv);
+                    o8.w = ptx::pack_bf16x2(acc[r][6] * inv, acc[r][7] * inv);
+                    *reinterpret_cast<uint4*>(p.out + ((int64_t)b * p.Sq * p.Hq + (int64_t)kvh * p.g) * kHeadDim +
+                                              roff[row] + dc * 8) = o8;
+                    if (LSE && dc == 0)
+                        p.lse_out[((int64_t)b * p.Hq + (int64_t)kvh * p.g) * p.Sq + row] =
+                            (den[r] > 0.f ? mx[r] + ptx::lg2(den[r]) : -INFINITY) * 0.6931471805599453f;
                 }
             }
             return true;
+        };
+
+        struct Pending {
+            int pc = -1;
+            int32_t b = 0, kvh = 0, n = 0;
+            float vsc = 1.f;
+            bool whole = false, is_first = false;
+        } pend;
+        // epilogue of piece P: O^T out of TMEM, row sums and maxima from shared memory,
+        // then the output rows (a whole unit) or a record and the arrival (a cut unit)
+        auto epilogue = [&](const Pending& P) -> bool {
+            const int ob = P.pc & 1;
+            if (!wait_all(OFULL(ob), (P.pc >> 1) & 1)) return false;
+            ptx::tc_fence_after();
+            const float* lp = lpart + ob * NP * 4;
+            const float* mp = mrefs + ob * NP;
+            auto lsum_of = [&](int r) {
+                const float4 l4 = ptx::lds_f4(ptx::smem_u32(lp + r * 4));
+                return (l4.x + l4.y) + (l4.z + l4.w);
+            };
+            const int64_t slot = P.whole ? 0 : slot_of(P.b, P.kvh, P.n);
+            // 16-bit rows for the output and for 32-row records, fp32 for 16-row records
+            const bool f32 = !P.whole && NP == 16;
+            // O^T streamed 16 columns (rows) at a time into the staging buffer
+#pragma unroll
+            for (int h = 0; h < NP / 16; ++h) {
+                float o16[16];
+                ptx::tc_ld16((tO0 + (uint32_t)(ob * NP + 16 * h)) | lane_off, o16);
+                ptx::tc_wait_ld();
+#pragma unroll
+                for (int r16 = 0; r16 < 16; ++r16) {
+                    const int r = 16 * h + r16;
+                    const float v = norm_of(o16[r16], lsum_of(r), P.vsc);
+                    if (f32) reinterpret_cast<float*>(stg)[r * kHeadDim + st] = v;
+                    else reinterpret_cast<__nv_bfloat16*>(stg)[r * kHeadDim + st] = __float2bfloat16_rn(v);
+                }
+            }
+            ptx::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) ptx::mbar_arrive(OFREE(ob));
+            // log2-sum-exp of row st (threads st < NP)
+            if (st < NP) {
+                const float l2 = lse2_of(mp[st], lsum_of(st));
+                if (!P.whole) p.rec_lse[slot * NP + st] = l2;
+                else if (LSE && st < p.rows)
+                    p.lse_out[((int64_t)P.b * p.Hq + (int64_t)P.kvh * p.g) * p.Sq + st] = l2 * 0.6931471805599453f;
+            }
+            if (!xsync()) return false;
+            // the staged rows leave in 16-byte pieces
+            const uint4* s4 = reinterpret_cast<const uint4*>(stg);
+            if (P.whole) {
+                __nv_bfloat16* obase = p.out + ((int64_t)P.b * p.Sq * p.Hq + (int64_t)P.kvh * p.g) * kHeadDim;
+                for (int k = st; k < NP * 16; k += 128) {
+                    const int r = k >> 4, c = k & 15;
+                    if (r < p.rows) *reinterpret_cast<uint4*>(obase + roff[r] + c * 8) = s4[k];
+                }
+            } else {
+                uint4* d4 = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.rec_o) +
+                                                     slot * (f32 ? NP * kHeadDim * 4 : NP * kHeadDim * 2));
+                for (int k = st; k < (f32 ? NP * 32 : NP * 16); k += 128) d4[k] = s4[k];
+            }
+            if (P.whole) return true;
+            return arrive_merge(P.b, P.kvh, P.n, true, P.is_first ? done_cut_first : done_cut_last);
         };
 
         Tile t;
@@ -768,17 +894,13 @@ pgqa_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
                 const int qb = pc & 1;
                 if (!wait_all(QFULL(qb), (pc >> 1) & 1)) { ok = false; break; }
 #pragma unroll
-                for (int r = 0; r < NP; ++r) mul[r] = mulv[qb * NP + r];
+                for (int r = 0; r < (KV8 ? NP : 1); ++r) mul[r] = mulv[qb * NP + r];
                 __syncwarp();
                 if (lane == 0) ptx::mbar_arrive(QFREE(qb));
 #pragma unroll
                 for (int r = 0; r < NP; ++r) { m_ref[r] = -INFINITY; l_part[r] = 0.f; }
                 if (KV8) vsc = (p.v_scale != nullptr) ? __ldg(p.v_scale + t.kvh) : 1.f;
-                if (MQ) {
-#pragma unroll
-                    for (int r = 0; r < NP; ++r)
-                        lim[r] = (!p.causal || r >= p.rows) ? t.L : t.L - p.Sq + (r - (r / p.Sq) * p.Sq) + 1;
-                }
+                causal_base = t.L - p.Sq + 1;
                 piece_c0 = t.c0;
             }
             const int32_t tok0 = t.c0 * kChunkTokens;
@@ -804,20 +926,11 @@ pgqa_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
                     for (int c = 0; c < 8; ++c) {  // 16 dims per 16-byte chunk
                         uint4 w8 = make_uint4(0, 0, 0, 0);
                         if (valid) w8 = ptx::lds_u4(src + (((uint32_t)c ^ sw) << 4));
-                        // alternate chunks on the conversion unit and on the integer
-                        // pipes, which then run side by side (ex2 needs the former too)
                         uint32_t h[8];
-                        if (c & 1) {
-                            ptx::e4m3x4_to_f16_alu(w8.x, h[0], h[1]);
-                            ptx::e4m3x4_to_f16_alu(w8.y, h[2], h[3]);
-                            ptx::e4m3x4_to_f16_alu(w8.z, h[4], h[5]);
-                            ptx::e4m3x4_to_f16_alu(w8.w, h[6], h[7]);
-                        } else {
-                            ptx::e4m3x4_to_f16(w8.x, h[0], h[1]);
-                            ptx::e4m3x4_to_f16(w8.y, h[2], h[3]);
-                            ptx::e4m3x4_to_f16(w8.z, h[4], h[5]);
-                            ptx::e4m3x4_to_f16(w8.w, h[6], h[7]);
-                        }
+                        ptx::e4m3x4_to_f16(w8.x, h[0], h[1]);
+                        ptx::e4m3x4_to_f16(w8.y, h[2], h[3]);
+                        ptx::e4m3x4_to_f16(w8.z, h[4], h[5]);
+                        ptx::e4m3x4_to_f16(w8.w, h[6], h[7]);
                         const uint32_t hb = dst + (uint32_t)((c >> 2) * G::kHalf);
                         const uint32_t cc = (uint32_t)(2 * (c & 3));
                         ptx::sts_u4(hb + ((cc ^ sw) << 4), make_uint4(h[0], h[1], h[2], h[3]));
@@ -833,10 +946,15 @@ pgqa_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
                 if (lane == 0) ptx::mbar_arrive(SFREE(sb));
 
             bool vote = false;
+            uint32_t vmask = st < nvalid ? 0xffffffffu : 0u;  // rows that see this key
+            if (MQ && p.causal) {
+                const int32_t k = pos - causal_base;
+                if (k >= 0) vmask = (st < nvalid && k < p.Sq - 1) ? vism[k] : 0u;
+            }
 #pragma unroll
             for (int r = 0; r < NP; ++r) {
-                const bool vis = (st < nvalid) && (!MQ || pos < lim[MQ ? r : 0]);
-                const float x = vis ? s[r] * mul[r] : -INFINITY;
+                const bool vis = (vmask >> r) & 1u;
+                const float x = vis ? s[r] * mul[KV8 ? r : 0] : -INFINITY;
                 s[r] = x;
                 vote = vote || (x > m_ref[r] + kLazyLog2);
             }
@@ -923,64 +1041,60 @@ pgqa_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
                 if (lane == 0) ptx::mbar_arrive(PFULL(sb));
 
             if (t.last) {
-                /* ---- epilogue of this CTA's piece of the unit ---- */
-                const int ob = pc & 1;
-                if (!wait_all(OFULL(ob), (pc >> 1) & 1)) { ok = false; break; }
-                ptx::tc_fence_after();
-                float o[NP];
-                tld(tO0 + (uint32_t)(ob * NP), o);
-                ptx::tc_wait_ld();
-                ptx::tc_fence_before();
-                __syncwarp();
-                if (lane == 0) ptx::mbar_arrive(OFREE(ob));
-                // l of each row: sum of the 128 token lanes' partial sums
-                float* rb = red + (xg_n & 1) * NP * 4;
+                /* ---- end of this CTA's piece of the unit: its per-warp row sums and its
+                 * reference maxima go to shared memory and its epilogue waits one tile (its
+                 * O^T buffer stays untouched until the piece after next), so the stream does
+                 * not stop for O^T to complete at every unit boundary ---- */
+                float* lp = lpart + (pc & 1) * NP * 4;
 #pragma unroll
                 for (int r = 0; r < NP; ++r) {
                     float v = l_part[r];
 #pragma unroll
                     for (int o2 = 16; o2 > 0; o2 >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o2);
-                    if (lane == 0) rb[r * 4 + wq] = v;
+                    if (lane == 0) lp[r * 4 + wq] = v;
                 }
-                if (!xsync()) { ok = false; break; }
-                float inv[NP], lse2[NP];
+                if (st == 0)
 #pragma unroll
-                for (int r = 0; r < NP; ++r) {
-                    const float4 l4 = ptx::lds_f4(ptx::smem_u32(rb + r * 4));
-                    const float l = (l4.x + l4.y) + (l4.z + l4.w);
-                    inv[r] = (!MQ || l > 0.f) ? vsc / l : 0.f;
-                    lse2[r] = (!MQ || l > 0.f) ? m_ref[r] + ptx::lg2(l) : -INFINITY;
-                }
-                const bool whole = (piece_c0 == 0) && (t.c0 + t.nc == t.n);
-                if (whole) {
-#pragma unroll
-                    for (int r = 0; r < NP; ++r) {
-                        if (r < p.rows) {
-                            p.out[row_offset<MQ>(p, t.b, t.kvh, r) + st] = __float2bfloat16_rn(o[r] * inv[r]);
-                            if (LSE && st == 0)
-                                p.lse_out[lse_index<MQ>(p, t.b, t.kvh, r)] = lse2[r] * 0.6931471805599453f;
-                        }
-                    }
-                } else {
-                    const bool is_first = cut_first && t.b == first_b && t.kvh == first_j && piece_c0 != 0;
-                    if (!finish_cut(t.b, t.kvh, t.n, o, inv, lse2, true,
-                                    is_first ? done_cut_first : done_cut_last)) { ok = false; break; }
-                }
+                    for (int r = 0; r < NP; ++r) mrefs[(pc & 1) * NP + r] = m_ref[r];
+                Pending nx;
+                nx.pc = pc;
+                nx.b = t.b;
+                nx.kvh = t.kvh;
+                nx.n = t.n;
+                nx.vsc = vsc;
+                nx.whole = (piece_c0 == 0) && (t.c0 + t.nc == t.n);
+                nx.is_first = cut_first && t.b == first_b && t.kvh == first_j && piece_c0 != 0;
+                // a piece still pending here had only this one tile after it
+                if (pend.pc >= 0 && !epilogue(pend)) { ok = false; break; }
+                pend = nx;
+            } else if (pend.pc >= 0 && pend.pc < pc) {
+                // one tile after a piece ended (its partials were stored before this tile's
+                // exchange, its last PV has long been issued): its epilogue runs now
+                if (!epilogue(pend)) { ok = false; break; }
+                pend.pc = -1;
             }
             ++i;
         }
+        if (ok && pend.pc >= 0) {
+            // the last piece's partials become visible to every warp at this exchange
+            ok = xsync() && epilogue(pend);
+        }
         if (!ok) {
             // a wait expired: still arrive on the counters of the units this slice cuts
-            float z[NP], ninf[NP];
-#pragma unroll
-            for (int r = 0; r < NP; ++r) { z[r] = 0.f; ninf[r] = -INFINITY; }
+            auto empty_record = [&](int32_t b, int32_t kvh, int32_t n) {
+                const int64_t slot = slot_of(b, kvh, n);
+                for (int r = 0; r < NP; ++r) put_rec(slot, r, 0.f);
+                if (st < NP) p.rec_lse[slot * NP + st] = -INFINITY;
+            };
             if (cut_first && !done_cut_first) {
                 const int32_t n = (int32_t)(pre[first_b + 1] - pre[first_b]);
-                finish_cut(first_b, first_j, n, z, z, ninf, false, done_cut_first);
+                empty_record(first_b, first_j, n);
+                arrive_merge(first_b, first_j, n, false, done_cut_first);
             }
             if (cut_last && !done_cut_last) {
                 const int32_t n = (int32_t)(pre[last_b + 1] - pre[last_b]);
-                finish_cut(last_b, last_j, n, z, z, ninf, false, done_cut_last);
+                empty_record(last_b, last_j, n);
+                arrive_merge(last_b, last_j, n, false, done_cut_last);
             }
         }
     }
