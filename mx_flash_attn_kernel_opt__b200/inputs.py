@@ -230,6 +230,36 @@ def baseline_config(name, seed=0, device="cpu", kv_head_range: Optional[tuple] =
                         scale=1.0 / math.sqrt(D), name=name, seqlen_k=cap)
 
 
+def golden_slice(name, index, seed=5):
+    """A reduced batch of workload `name`: the sequences at `index` (their lengths), with
+    the workload's head layout, page size and value distribution, a randomly permuted
+    table and a pool of exactly len(index) x row-width pages (the reference ABI's pool =
+    batch x row width; the pages no sequence uses stay in the pool).  Used for golden
+    vectors of the reference's own operator at the benchmark's shapes."""
+    cfg = CONFIGS[name]
+    L_all, _ = config_seq_lens(name)
+    lens = [int(L_all[i]) for i in index]
+    P = cfg["P"]
+    npg = [(L + P - 1) // P for L in lens]
+    width = max(npg)
+    spare = len(lens) * width - sum(npg)
+    inp = custom_case(len(lens), cfg["Hq"], cfg["Hkv"], P, lens, seed=seed, table="permuted",
+                      spare_pages=spare, width=width, std_kv=0.5 if name == "c4" else 1.0)
+    inp.name = f"{name}_slice"
+    return inp
+
+
+def golden_slice_index(name):
+    """The sequences the golden slices keep: c3 its first 8; c4 its shortest, median,
+    90th-percentile and longest (its lengths are log-uniform over [64, 65536])."""
+    L_all, _ = config_seq_lens(name)
+    if name == "c3":
+        return list(range(8))
+    order = torch.argsort(L_all.to(torch.int64)).tolist()
+    n = len(order)
+    return [order[0], order[n // 2], order[(9 * n) // 10], order[-1]]
+
+
 # --------------------------------------------------------------------------------------
 # The reference's correctness table
 # --------------------------------------------------------------------------------------

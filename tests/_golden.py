@@ -14,6 +14,8 @@ def make_inputs(spec):
     from mx_flash_attn_kernel_opt__b200 import inputs
     if spec["kind"] == "spj":
         inp = inputs.spj_case(spec["case"], table=spec["table"])
+    elif spec["kind"] == "slice":
+        inp = inputs.golden_slice(spec["config"], spec["index"])
     else:
         inp = inputs.baseline_config(spec["config"])
     if spec.get("poison"):

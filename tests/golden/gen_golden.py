@@ -10,8 +10,13 @@ it treat them as numbers (bf16 dots as exact fp32 products with fp32 accumulatio
 tensor core does; elementwise bf16 arithmetic and fp32 -> bf16 casts rounded to nearest).
 
 Inputs come from mx_flash_attn_kernel_opt__b200.inputs (seeded CPU generators, so the
-tests regenerate the same bytes; manifest.json records a sha256 of every input).  Only
-the first rows of each output are stored, as bf16 bit patterns.
+tests regenerate the same bytes; manifest.json records a sha256 of every input).  Every
+row of each output is stored, as bf16 bit patterns.
+
+Cases: the reference's 14-case table (verify_real.py:8-10) with contiguous and permuted
+tables, benchmark config c1 whole, reduced-batch slices of c3 (its first 8 sequences)
+and c4 (g = 7, P = 64: its shortest, median, 90th-percentile and longest sequences) at
+the benchmark's shapes, and a NaN-poisoned pool.
 
 Run (needs the reference checkout; not needed by the tests):
     python tests/golden/gen_golden.py --reference /path/to/reference [cases...]
@@ -24,7 +29,6 @@ import time
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
-ROWS_KEPT = 4
 
 
 def _patch_interpreter_bf16():
@@ -110,6 +114,11 @@ def cases():
     for c in (3, 5, 8, 11):
         out.append({"name": f"spj{c:02d}_perm", "kind": "spj", "case": c, "table": "permuted"})
     out.append({"name": "c1", "kind": "config", "config": "c1"})
+    sys.path.insert(0, REPO)
+    from mx_flash_attn_kernel_opt__b200 import inputs
+    for cfg in ("c3", "c4"):
+        out.append({"name": f"{cfg}_slice", "kind": "slice", "config": cfg,
+                    "index": inputs.golden_slice_index(cfg)})
     out.append({"name": "spj05_poison", "kind": "spj", "case": 5, "table": "permuted",
                 "poison": True})
     return out
@@ -120,6 +129,8 @@ def make_inputs(spec):
     from mx_flash_attn_kernel_opt__b200 import inputs
     if spec["kind"] == "spj":
         inp = inputs.spj_case(spec["case"], table=spec["table"])
+    elif spec["kind"] == "slice":
+        inp = inputs.golden_slice(spec["config"], spec["index"])
     else:
         inp = inputs.baseline_config(spec["config"])
     if spec.get("poison"):
@@ -159,7 +170,7 @@ def main():
         ref.run_kernel(inp.q.view(B, 1, Hq, D), inp.k, inp.v, out, inp.seq_lens,
                        inp.block_table, B, inp.seqlen_k, 1, Hq, Hkv, D, P, nb, 0)
         dt = time.time() - t0
-        rows = list(range(min(B, ROWS_KEPT)))
+        rows = list(range(B))
         bits = out[rows, 0].contiguous().view(torch.int16).numpy().astype(np.uint16)
         np.savez_compressed(os.path.join(HERE, spec["name"] + ".npz"), rows=np.array(rows),
                             out_bf16_bits=bits)

@@ -94,13 +94,15 @@ def test_baseline_config_vs_oracle(name, cuda_device):
 
 
 def test_c5_full_size_sampled_rows_and_page_permutation(cuda_device):
-    """c5 at full size (~34 GB): sampled sequences against the oracle, and bit-identical
-    output after moving every page to another physical slot (indexing is exact)."""
+    """c5 at full size (~34 GB): 32 sequences spread over all 512 (every 16th, starting at
+    a different offset in each half) against the oracle, and bit-identical output after
+    moving every page to another physical slot (indexing is exact)."""
     dev = cuda_device
     inp = inputs.baseline_config("c5", device=dev)
     out = pgqa.decode(inp.q, inp.k, inp.v, inp.block_table, inp.seq_lens, scale=inp.scale)
     torch.cuda.synchronize()
-    rows = [0, 1, 255, 511]
+    rows = list(range(0, 256, 16)) + list(range(263, 512, 16))
+    assert len(rows) == 32 and rows[-1] == 503
     P = inp.page_size
     for b in rows:
         L = int(inp.seq_lens[b])
