@@ -146,8 +146,9 @@ __device__ __forceinline__ Cursor locate(const DecodeParams& p, const uint32_t* 
     cu.b = find_seq(pre, p.B, p.U, x);
     cu.n = (int32_t)(pre[cu.b + 1] - pre[cu.b]);
     const int64_t r = x - (int64_t)pre[cu.b] * p.U;
-    cu.j = (int32_t)(r / cu.n);
+    cu.j = (r <= kSmallProduct) ? (int32_t)((uint32_t)r / (uint32_t)cu.n) : (int32_t)(r / cu.n);
     cu.c = (int32_t)(r - (int64_t)cu.j * cu.n);
+    // read here, first needed only once the first tiles are in flight
     cu.L = clamp_len(keys_of(p, cu.b), p.cap_tokens);
     return cu;
 }
@@ -363,6 +364,9 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
      * that writes lengths or table only makes the prefetch miss.  Table entries are read
      * only below ceil(L/P) of the clamped length (inside every row by the table's
      * contract) and page ids outside [0, num_pages) are not prefetched. */
+    // the warp's first block-table window as the pass located it (sequence, first page,
+    // pages of the sequence; sp_b < 0: none)
+    int32_t sp_b = -1, sp_p0 = 0, sp_npg = 0;
     if (p.spec_chunks > 0) {
         scan_prefix([&](int b) { return ptx::ld_cg_s32(p.seq_lens + b) + p.debug_spec_skew; });
         const int64_t T = (int64_t)pre[p.B] * p.U;
@@ -380,7 +384,7 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
                 int32_t b = find_seq(pre, p.B, p.U, ws);
                 int32_t n = (int32_t)(pre[b + 1] - pre[b]);
                 const int64_t r = ws - (int64_t)pre[b] * p.U;
-                int32_t j = (int32_t)(r / n);
+                int32_t j = (r <= kSmallProduct) ? (int32_t)((uint32_t)r / (uint32_t)n) : (int32_t)(r / n);
                 int32_t c = (int32_t)(r - (int64_t)j * n);
                 int32_t win_b = -1, win_p0 = 0, win_pid = 0;
                 for (int64_t k = 0; k < npf; ++k) {
@@ -393,6 +397,7 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
                         win_pid = (pg < npg)
                                       ? ptx::ld_cg_s32(p.block_table + (int64_t)b * p.bt_stride + pg)
                                       : -1;
+                        if (k == 0) { sp_b = b; sp_p0 = page; sp_npg = npg; }
                     }
                     const int32_t pid = __shfl_sync(0xffffffffu, win_pid, page - win_p0);
                     if (lane == 0 && (uint32_t)pid < (uint32_t)p.num_pages) {
@@ -423,9 +428,17 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
     // is used after it.
     ptx::griddep_wait();
 
+    // The warp's first window is read again now (the pass's values may be stale), in the
+    // same round trip as the lengths check; it is used when the partition is unchanged,
+    // so the first tiles wait for no further load.
+    int32_t sp_pid = 0;
+    if (sp_b >= 0) {
+        const int32_t pg = sp_p0 + lane;
+        sp_pid = (pg < sp_npg) ? __ldg(p.block_table + (int64_t)sp_b * p.bt_stride + pg) : 0;
+    }
+    bool rebuild = true;
     {
         int32_t bad = 0;
-        bool rebuild = true;
         if (p.spec_chunks > 0) {
             int32_t changed = 0;
             for (int b = sb0; b < sb1; ++b) {
@@ -446,12 +459,15 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
         if (bad && blockIdx.x == 0) atomicOr(p.err, kErrBadSeqlen);
     }
 
-    /* Zero-length sequences produce zeros (softmax over an empty set), written by CTA 0. */
+    /* Zero-length sequences produce zeros (softmax over an empty set) and a log-sum-exp of
+     * -inf, written by CTA 0. */
     if (blockIdx.x == 0) {
         for (int b = tid; b < p.B; b += NT) {
             if (pre[b + 1] == pre[b]) {
                 uint4* o4 = reinterpret_cast<uint4*>(p.out + (int64_t)b * p.Sq * p.Hq * kHeadDim);
                 for (int i = 0; i < p.Sq * p.Hq * kHeadDim / 8; ++i) o4[i] = make_uint4(0, 0, 0, 0);
+                if (LSE)
+                    for (int i = 0; i < p.Hq * p.Sq; ++i) p.lse_out[(int64_t)b * p.Hq * p.Sq + i] = -INFINITY;
             }
         }
     }
@@ -495,13 +511,20 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
         int32_t ipage = (ic.c * kChunkTokens) / P;
         int32_t ioff = ic.c * kChunkTokens - ipage * P;
         int32_t ikvh = ic.j / p.n_w;
+        if (!rebuild && ic.b == sp_b && ipage == sp_p0) {  // the window read after the wait
+            win_b = sp_b;
+            win_p0 = sp_p0;
+            win_pid = sp_pid;
+        }
 
         auto issue_next = [&]() {
             const int32_t page = ipage;
             if (ic.b != win_b || page < win_p0 || page >= win_p0 + 32) {
                 win_b = ic.b;
                 win_p0 = page;
-                const int32_t npg = (ic.L + P - 1) / P;
+                // pages of the sequence, ceil(L / P) = ceil(16 n / P) as P is a multiple
+                // of 16 (from the chunk count, so the window does not wait for L)
+                const int32_t npg = (ic.n * kChunkTokens + P - 1) / P;
                 const int32_t pg = page + lane;
                 win_pid = (pg < npg) ? __ldg(p.block_table + (int64_t)ic.b * p.bt_stride + pg) : 0;
             }

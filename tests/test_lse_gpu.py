@@ -113,3 +113,37 @@ def test_lse_with_appended_tokens(cuda_device):
     torch.cuda.synchronize()
     assert_parity(out, ref, what="append")
     assert_lse(lse, ref_lse, "append")
+
+
+@pytest.mark.parametrize("Sq", [1, 3])
+def test_lse_zero_length_sequences(Sq, cuda_device):
+    """Sequences with no keys give zeros and a log-sum-exp of -inf in every row.  Both
+    buffers hold NaN when the kernel starts (out is passed in; the LSE buffer is a
+    NaN-filled block of the same size handed back by the caching allocator), so an entry
+    the kernel skipped would show."""
+    lens = [0, 300, 0, 17]
+    inp = inputs.custom_case(4, 32, 8, 16, lens, seed=71 + Sq)
+    q = inp.q
+    if Sq > 1:
+        g = torch.Generator().manual_seed(72)
+        q = torch.randn(4, Sq, 32, 128, generator=g).to(torch.bfloat16)
+    ref, ref_lse = paged_decode_ref(q, inp.k, inp.v, inp.block_table, inp.seq_lens,
+                                    causal=Sq > 1, return_lse=True)
+    d = inp.to(cuda_device)
+    qd = q.to(cuda_device)
+    # a first call creates the cached workspace, so that the loop's only allocation
+    # between freeing the poison and the kernel is the LSE buffer
+    pgqa.decode(qd, d.k, d.v, d.block_table, d.seq_lens, causal=Sq > 1, return_lse=True)
+    for _ in range(2):
+        out = torch.full_like(qd, float("nan"))
+        poison = torch.full((4, 32, Sq), float("nan"), device=cuda_device)
+        poison_ptr = poison.data_ptr()
+        del poison
+        out, lse = pgqa.decode(qd, d.k, d.v, d.block_table, d.seq_lens, out=out,
+                               causal=Sq > 1, return_lse=True)
+        torch.cuda.synchronize()
+        assert lse.data_ptr() == poison_ptr, "the LSE buffer was not the poisoned block"
+        assert_parity(out, ref, edge=Sq > 1, what=f"empty Sq={Sq}")
+        assert_lse(lse, ref_lse, f"empty Sq={Sq}")
+        assert torch.isneginf(lse[0]).all() and torch.isneginf(lse[2]).all()
+        assert (out[0] == 0).all() and (out[2] == 0).all()
