@@ -97,6 +97,7 @@ struct DecodeParams {
     const float* k_scale;  // FP8 pools: dequantisation factor per KV head (null = 1)
     const float* v_scale;
     int32_t page_size, bt_stride, num_pages;
+    int32_t page_shift;  // log2(page_size) when it is a power of two, else -1
     int64_t cap_tokens;  // bt_stride * page_size (clamp for seq_lens)
     float scale_log2;    // scale * log2(e)
     int32_t min_chunks;
@@ -141,16 +142,27 @@ __device__ __forceinline__ int32_t find_seq(const uint32_t* pre, int32_t B, int6
     return lo;
 }
 
-__device__ __forceinline__ Cursor locate(const DecodeParams& p, const uint32_t* pre, int64_t x) {
+/* Cursor of flat chunk x from the prefix table alone (L left 0: no global read). */
+__device__ __forceinline__ Cursor locate_chunk(const DecodeParams& p, const uint32_t* pre, int64_t x) {
     Cursor cu;
     cu.b = find_seq(pre, p.B, p.U, x);
     cu.n = (int32_t)(pre[cu.b + 1] - pre[cu.b]);
     const int64_t r = x - (int64_t)pre[cu.b] * p.U;
     cu.j = (r <= kSmallProduct) ? (int32_t)((uint32_t)r / (uint32_t)cu.n) : (int32_t)(r / cu.n);
     cu.c = (int32_t)(r - (int64_t)cu.j * cu.n);
-    // read here, first needed only once the first tiles are in flight
+    cu.L = 0;
+    return cu;
+}
+
+__device__ __forceinline__ Cursor locate(const DecodeParams& p, const uint32_t* pre, int64_t x) {
+    Cursor cu = locate_chunk(p, pre, x);
     cu.L = clamp_len(keys_of(p, cu.b), p.cap_tokens);
     return cu;
+}
+
+/* Page index of token offset t inside a sequence (a shift when P is a power of two). */
+__device__ __forceinline__ int32_t page_of(const DecodeParams& p, int32_t t) {
+    return p.page_shift >= 0 ? (t >> p.page_shift) : t / p.page_size;
 }
 
 /* Step to the next chunk.  Must only be called when a next chunk exists. */
@@ -318,6 +330,7 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
     const int gid = lane >> 2;  // MMA group id (row within an 8-row block)
     const int tig = lane & 3;   // thread in group
 
+    const uint64_t pol = ptx::policy_evict_first();
     if (tid == 0) {
         ptx::prefetch_tensormap(&kmap);
         ptx::prefetch_tensormap(&vmap);
@@ -367,32 +380,47 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
     // the warp's first block-table window as the pass located it (sequence, first page,
     // pages of the sequence; sp_b < 0: none)
     int32_t sp_b = -1, sp_p0 = 0, sp_npg = 0;
+
+    /* The partition of the call from the prefix table: T flat chunks, nct active CTAs,
+     * this CTA's slice [cs, ce) over wa active warps, this warp's slice [ws, we) and the
+     * cursor of its first chunk (length not read yet).  Computed by the pass before
+     * griddepcontrol.wait and kept when the lengths check finds the same chunk counts,
+     * else computed after it. */
+    int64_t T = 0, nct = 0, cs = 0, ce = 0, ws = 0, we = 0;
+    int wa = 0;
+    Cursor ic0{};
+    auto partition = [&]() {
+        T = (int64_t)pre[p.B] * p.U;
+        nct = T > 0 ? active_ctas(T, gridDim.x, W, p.min_chunks) : 0;
+        wa = 0;
+        if ((int64_t)blockIdx.x >= nct) return;
+        cs = slice_begin(blockIdx.x, nct, T);
+        ce = slice_begin(blockIdx.x + 1, nct, T);
+        wa = (int)active_warps(ce - cs, W);
+        if (warp < wa) {
+            ws = cs + slice_begin(warp, wa, ce - cs);
+            we = cs + slice_begin(warp + 1, wa, ce - cs);
+            ic0 = locate_chunk(p, pre, ws);
+        }
+    };
+
     if (p.spec_chunks > 0) {
         scan_prefix([&](int b) { return ptx::ld_cg_s32(p.seq_lens + b) + p.debug_spec_skew; });
-        const int64_t T = (int64_t)pre[p.B] * p.U;
-        const int64_t nct = T > 0 ? active_ctas(T, gridDim.x, W, p.min_chunks) : 0;
+        partition();
         // the table may be far longer than the sequences: the prefetch needs real length
-        if ((int64_t)blockIdx.x < nct && T >= p.spec_min_total) {
-            const int64_t cs = slice_begin(blockIdx.x, nct, T);
-            const int64_t clen = slice_begin(blockIdx.x + 1, nct, T) - cs;
-            const int wa = (int)active_warps(clen, W);
-            if (warp < wa) {
-                const int64_t ws = cs + slice_begin(warp, wa, clen);
-                const int64_t ntot = cs + slice_begin(warp + 1, wa, clen) - ws;
+        if (warp < wa && T >= p.spec_min_total) {
+            {
+                const int64_t ntot = we - ws;
                 const int64_t npf = ntot < p.spec_chunks ? ntot : p.spec_chunks;
                 const int P = p.page_size;
-                int32_t b = find_seq(pre, p.B, p.U, ws);
-                int32_t n = (int32_t)(pre[b + 1] - pre[b]);
-                const int64_t r = ws - (int64_t)pre[b] * p.U;
-                int32_t j = (r <= kSmallProduct) ? (int32_t)((uint32_t)r / (uint32_t)n) : (int32_t)(r / n);
-                int32_t c = (int32_t)(r - (int64_t)j * n);
+                int32_t b = ic0.b, n = ic0.n, j = ic0.j, c = ic0.c;
                 int32_t win_b = -1, win_p0 = 0, win_pid = 0;
                 for (int64_t k = 0; k < npf; ++k) {
-                    const int32_t page = (c * kChunkTokens) / P;
+                    const int32_t page = page_of(p, c * kChunkTokens);
                     if (b != win_b || page < win_p0 || page >= win_p0 + 32) {
                         win_b = b;
                         win_p0 = page;
-                        const int32_t npg = (n * kChunkTokens + P - 1) / P;
+                        const int32_t npg = page_of(p, n * kChunkTokens + P - 1);
                         const int32_t pg = page + lane;
                         win_pid = (pg < npg)
                                       ? ptx::ld_cg_s32(p.block_table + (int64_t)b * p.bt_stride + pg)
@@ -401,7 +429,7 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
                     }
                     const int32_t pid = __shfl_sync(0xffffffffu, win_pid, page - win_p0);
                     if (lane == 0 && (uint32_t)pid < (uint32_t)p.num_pages) {
-                        const int32_t kvh = j / p.n_w;
+                        const int32_t kvh = (p.n_w == 1) ? j : j / p.n_w;
                         const int32_t z = pid * P + (c * kChunkTokens - page * P);
                         ptx::tma_prefetch_l2_3d(&kmap, 0, kvh, z);
                         ptx::tma_prefetch_l2_3d(&vmap, 0, kvh, z);
@@ -458,6 +486,7 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
         }
         if (bad && blockIdx.x == 0) atomicOr(p.err, kErrBadSeqlen);
     }
+    if (rebuild) partition();
 
     /* Zero-length sequences produce zeros (softmax over an empty set) and a log-sum-exp of
      * -inf, written by CTA 0. */
@@ -472,19 +501,11 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
         }
     }
 
-    const int64_t U = p.U;
-    const int64_t T = (int64_t)pre[p.B] * U;
     if (T == 0) return;
-    const int64_t nct = active_ctas(T, gridDim.x, W, p.min_chunks);
     if ((int64_t)blockIdx.x >= nct) return;
-    const int64_t cs = slice_begin(blockIdx.x, nct, T);
-    const int64_t ce = slice_begin(blockIdx.x + 1, nct, T);
-    const int64_t clen = ce - cs;
-    const int wa = (int)active_warps(clen, W);
 
     const uint32_t ring_base = ptx::smem_u32(ring);
     const uint32_t bar_base = ptx::smem_u32(bars);
-    const uint64_t pol = ptx::policy_evict_first();
 
     /* Per-warp streaming state kept until the CTA-level merge (per row group grp). */
     bool have_first = false, have_last = false;
@@ -496,11 +517,10 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
     bool aborted = false;
 
     if (warp < wa) {
-        const int64_t ws = cs + slice_begin(warp, wa, clen);
-        const int64_t we = cs + slice_begin(warp + 1, wa, clen);
         const int64_t ntot = we - ws;
 
-        Cursor ic = locate(p, pre, ws);
+        Cursor ic = ic0;
+        ic.L = clamp_len(keys_of(p, ic.b), p.cap_tokens);  // first needed after the first issues
         Cursor cc = ic;
 
         int32_t win_b = -1, win_p0 = 0, win_pid = 0;
@@ -508,9 +528,9 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
         const int P = p.page_size;
         // page / slot of the issue cursor's chunk and its KV head, stepped with the cursor
         // (no division per chunk: chunks are 16-token aligned and P is a multiple of 16)
-        int32_t ipage = (ic.c * kChunkTokens) / P;
+        int32_t ipage = page_of(p, ic.c * kChunkTokens);
         int32_t ioff = ic.c * kChunkTokens - ipage * P;
-        int32_t ikvh = ic.j / p.n_w;
+        int32_t ikvh = (p.n_w == 1) ? ic.j : ic.j / p.n_w;
         if (!rebuild && ic.b == sp_b && ipage == sp_p0) {  // the window read after the wait
             win_b = sp_b;
             win_p0 = sp_p0;
@@ -524,7 +544,7 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
                 win_p0 = page;
                 // pages of the sequence, ceil(L / P) = ceil(16 n / P) as P is a multiple
                 // of 16 (from the chunk count, so the window does not wait for L)
-                const int32_t npg = (ic.n * kChunkTokens + P - 1) / P;
+                const int32_t npg = page_of(p, ic.n * kChunkTokens + P - 1);
                 const int32_t pg = page + lane;
                 win_pid = (pg < npg) ? __ldg(p.block_table + (int64_t)ic.b * p.bt_stride + pg) : 0;
             }
@@ -1651,6 +1671,9 @@ int decode_impl(const void* q, const void* k, const void* v, void* out, const in
     p.k_scale = k_scale;
     p.v_scale = v_scale;
     p.page_size = (int32_t)P;
+    p.page_shift = -1;
+    for (int sh = 0; sh < 31; ++sh)
+        if (((int64_t)1 << sh) == P) p.page_shift = sh;
     p.bt_stride = (int32_t)bt_stride;
     p.num_pages = (int32_t)num_pages;
     p.cap_tokens = cap;

@@ -67,7 +67,10 @@ PGQA_HD int64_t slice_owner(int64_t x, int64_t n, int64_t total) {
 /* Number of active CTAs for `total` chunks: every active warp gets at least
  * `min_chunks` chunks unless the whole problem is smaller than one CTA's share. */
 PGQA_HD int64_t active_ctas(int64_t total, int64_t grid, int64_t warps, int64_t min_chunks) {
-    int64_t n = total / (warps * min_chunks);
+    const int64_t per = warps * min_chunks;
+    int64_t n = (total <= kSmallProduct && per <= kSmallProduct)
+                    ? (int64_t)((uint32_t)total / (uint32_t)per)
+                    : total / per;
     if (n > grid) n = grid;
     if (n < 1) n = 1;
     return n;
