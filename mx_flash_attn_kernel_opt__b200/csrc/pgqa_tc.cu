@@ -307,6 +307,10 @@ pgqa_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
     };
 
     ptx::griddep_wait();
+    // The next kernel in the stream may be scheduled from now on: its CTAs take SMs only
+    // as this grid's CTAs leave them, and it waits for this grid's completion before it
+    // reads memory, so its launch and prologue overlap this grid's tail.
+    ptx::griddep_launch_dependents();
 
     /* ---- chunk prefix over sequences (every CTA; thread tid owns [sb0_, sb1_)) ---- */
     {
@@ -1099,7 +1103,6 @@ pgqa_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
         }
     }
 
-    ptx::griddep_launch_dependents();
     ptx::tc_fence_before();
     __syncthreads();
     if (warp == 3) {
