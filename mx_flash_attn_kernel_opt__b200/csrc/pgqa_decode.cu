@@ -1740,6 +1740,7 @@ int decode_impl(const void* q, const void* k, const void* v, void* out, const in
         t.k_scale = p.k_scale;
         t.v_scale = p.v_scale;
         t.page_size = p.page_size;
+        t.page_shift = p.page_shift;
         t.bt_stride = p.bt_stride;
         t.num_pages = p.num_pages;
         t.cap_tokens = p.cap_tokens;

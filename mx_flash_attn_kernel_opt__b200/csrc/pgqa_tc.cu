@@ -120,7 +120,7 @@ struct Walker {
             b = find_seq(pre, p.B, p.Hkv, cs);
             n = (int32_t)(pre[b + 1] - pre[b]);
             const int64_t r = cs - (int64_t)pre[b] * p.Hkv;
-            j = (int32_t)(r / n);
+            j = (r <= kSmallProduct) ? (int32_t)((uint32_t)r / (uint32_t)n) : (int32_t)(r / n);
             c = (int32_t)(r - (int64_t)j * n);
             L = clamp_len((int64_t)__ldg(p.seq_lens + b) + p.len_add, p.cap_tokens);
         }
@@ -177,9 +177,10 @@ struct Smem {
     static constexpr int kPOff = kQOff + 2 * kQ;
     static constexpr int kV16Off = kPOff + 2 * kP;
     static constexpr int kBarOff = kV16Off + 2 * kV16;
-    static constexpr int kBars = 2 * SK + 2 * SV + 18;
+    static constexpr int kBars = 2 * SK + 2 * SV + 20;
     static constexpr int kMiscOff = (kBarOff + kBars * 8 + 15) / 16 * 16;
-    // misc: [0] TMEM base, [4] abort flag, [16..48) warp sums, [48..80) exchange words
+    // misc: [0] TMEM base, [4] abort flag, [8] warp 2's arrival outcome, [16..48) warp sums,
+    // [48..80) exchange words
     // [2][4], then red[2][NP][4] f32, mul[2][NP] f32, row offsets and causal masks [NP] each,
     // then the prefix table
     static constexpr int kRedOff = kMiscOff + 80;
@@ -214,6 +215,8 @@ pgqa_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
     const uint32_t bars = sb0 + L::kBarOff;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMiscOff);
     volatile int32_t* abort_flag = reinterpret_cast<volatile int32_t*>(smem + L::kMiscOff + 4);
+    // 0: warp 2 did not arrive for the first cut unit, 1: it did, 2: it did and was last
+    volatile int32_t* w2flag = reinterpret_cast<volatile int32_t*>(smem + L::kMiscOff + 8);
     int32_t* wsum = reinterpret_cast<int32_t*>(smem + L::kMiscOff + 16);
     volatile int32_t* xword = reinterpret_cast<volatile int32_t*>(smem + L::kMiscOff + 48);  // [2][4]
     float* red = reinterpret_cast<float*>(smem + L::kRedOff);    // [2][NP][4]
@@ -240,6 +243,8 @@ pgqa_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
     auto QFREE = [&](int b) { return bars + 8u * (B2 + 14 + b); };
     const uint32_t XG = bars + 8u * (B2 + 16);       // softmax-group exchange
     const uint32_t MMADONE = bars + 8u * (B2 + 17);  // every MMA issued has completed
+    const uint32_t RECDONE = bars + 8u * (B2 + 18);  // the slice's first cut record is stored
+    const uint32_t W2DONE = bars + 8u * (B2 + 19);   // warp 2 has arrived for it (or given up)
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
@@ -270,7 +275,10 @@ pgqa_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
         }
         ptx::mbar_init(XG, 4);
         ptx::mbar_init(MMADONE, 1);
+        ptx::mbar_init(RECDONE, 4);
+        ptx::mbar_init(W2DONE, 1);
         *abort_flag = 0;
+        *w2flag = 0;
         ptx::fence_mbar_init();
     }
 
@@ -305,6 +313,24 @@ pgqa_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
         const bool ok = wait_bar(bar, parity);
         return __all_sync(0xffffffffu, ok);
     };
+
+    if (tid < NP) {
+        // row r of a KV head = (head r / Sq, token r % Sq): its offset in q / out relative
+        // to (sequence b, KV head kvh), and the rows a key at distance k past
+        // L - Sq + 1 stays visible to under the causal mask (bit r set: r % Sq > k).
+        // From the parameters alone, so it runs before the wait.
+        const int h = MQ ? tid / p.Sq : tid, i = MQ ? tid - (tid / p.Sq) * p.Sq : 0;
+        roff[tid] = (i * p.Hq + h) * kHeadDim;
+        uint32_t m = 0;
+        if (MQ) {
+            int rm = 0;  // r % Sq
+            for (int r = 0; r < NP; ++r) {
+                if (rm > tid) m |= 1u << r;
+                if (++rm == p.Sq) rm = 0;
+            }
+        }
+        vism[tid] = m;
+    }
 
     ptx::griddep_wait();
     // The next kernel in the stream may be scheduled from now on: its CTAs take SMs only
@@ -363,17 +389,6 @@ pgqa_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
         ptx::tmem_alloc(ptx::smem_u32(tmem_slot), kTmemCols);
         ptx::tmem_relinquish();
     }
-    if (tid < NP) {
-        // row r of a KV head = (head r / Sq, token r % Sq): its offset in q / out relative
-        // to (sequence b, KV head kvh), and the rows a key at distance k past
-        // L - Sq + 1 stays visible to under the causal mask (bit r set: r % Sq > k)
-        const int h = MQ ? tid / p.Sq : tid, i = MQ ? tid - (tid / p.Sq) * p.Sq : 0;
-        roff[tid] = (i * p.Hq + h) * kHeadDim;
-        uint32_t m = 0;
-        for (int r = 0; r < NP; ++r)
-            if (MQ && (r - (r / p.Sq) * p.Sq) > tid) m |= 1u << r;
-        vism[tid] = m;
-    }
     ptx::tc_fence_before();
     __syncthreads();
     ptx::tc_fence_after();
@@ -393,22 +408,24 @@ pgqa_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
         int it = 0;
         int32_t win_b = -1, win_p0 = 0, win_pid = 0;
         const int P = p.page_size;
+        auto page_of = [&](int32_t tok) { return p.page_shift >= 0 ? (tok >> p.page_shift) : tok / P; };
         while (w.next(p, t)) {
             const int slot = it % NS;
             const uint32_t empty = isK ? KEMPTY(slot) : VEMPTY(slot);
             if (it >= NS && !wait_bar(empty, ((it / NS) - 1) & 1)) break;
-            const int32_t page0 = (t.c0 * kChunkTokens) / P;
-            const int32_t pageN = ((t.c0 + t.nc - 1) * kChunkTokens) / P;
+            const int32_t page0 = page_of(t.c0 * kChunkTokens);
+            const int32_t pageN = page_of((t.c0 + t.nc - 1) * kChunkTokens);
             if (t.b != win_b || page0 < win_p0 || pageN >= win_p0 + 32) {
                 win_b = t.b;
                 win_p0 = page0;
-                const int32_t npg = (t.L + P - 1) / P;
+                // ceil(L / P) = ceil(16 n / P) (P a multiple of 16): no wait for the length
+                const int32_t npg = page_of(t.n * kChunkTokens + P - 1);
                 const int32_t pg = page0 + lane;
                 win_pid = (pg < npg) ? __ldg(p.block_table + (int64_t)t.b * p.bt_stride + pg) : 0;
             }
             const int k = lane < t.nc ? lane : 0;
             const int32_t tok = (t.c0 + k) * kChunkTokens;
-            const int32_t page = tok / P;
+            const int32_t page = page_of(tok);
             int32_t pid = __shfl_sync(0xffffffffu, win_pid, page - win_p0);
             const uint32_t bar = isK ? KFULL(slot) : VFULL(slot);
             if (lane == 0) {
@@ -555,11 +572,45 @@ pgqa_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
         /* ================= Q loader ================= */
         Walker w;
         w.init(p, pre, cs, ce);
+        /* The slice's first cut unit, when another piece follows it here: the softmax
+         * group stores its record mid-stream (RECDONE) and this warp makes the arrival on
+         * the unit's counter (release, atomic; for a last arrival the reset and acquire),
+         * so that the stream does not wait for those round trips.  The outcome goes to
+         * w2flag and W2DONE, which the softmax group reads after its stream. */
+        const int32_t fb = w.b, fj = w.j, fn = w.n;
+        const int64_t fbeg = (int64_t)pre[fb] * p.Hkv + (int64_t)fj * fn;
+        bool first_pending = (w.c != 0) && (fbeg + fn < ce);
+        auto first_arrive = [&](bool got) {
+            int32_t f = 0;
+            if (got && lane == 0) {
+                const int64_t c_first = slice_owner(fbeg, nct, T);
+                const int64_t c_last = slice_owner(fbeg + fn - 1, nct, T);
+                int32_t* cnt = p.counters + (int64_t)fb * p.Hkv + fj;
+                // the record stores, ordered before this thread by RECDONE (cumulative)
+                ptx::fence_acq_rel_gpu();
+                const int32_t prev = ptx::atom_add_acq_rel_gpu(cnt, 1);
+                f = 1;
+                if (prev == (int32_t)(c_last - c_first)) {
+                    *cnt = 0;
+                    ptx::fence_acq_rel_gpu();  // the other CTAs' records, for the merge
+                    f = 2;
+                }
+            }
+            if (lane == 0) {
+                *w2flag = f;
+                ptx::mbar_arrive(W2DONE);
+            }
+            __syncwarp();
+            first_pending = false;
+        };
         Tile t;
         int pc = 0;
         while (w.next(p, t)) {
             if (!t.first) continue;
             const int qb = pc & 1;
+            // a record handed over since the last look is released before the next wait
+            if (first_pending && __shfl_sync(0xffffffffu, lane == 0 && ptx::mbar_test_wait(RECDONE, 0) ? 1 : 0, 0))
+                first_arrive(true);
             if (pc >= 2 && !wait_all(QFREE(qb), ((pc >> 1) - 1) & 1)) break;
             const uint32_t qs = qbuf + (uint32_t)qb * L::kQ;
             const int r = lane;
@@ -628,6 +679,7 @@ pgqa_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
             if (lane == 0) ptx::mbar_arrive(QFULL(qb));
             ++pc;
         }
+        if (first_pending) first_arrive(wait_all(RECDONE, 0));  // gives up only on an abort
     } else if (warp >= 4) {
         /* ================= softmax and epilogue (128 threads) ================= */
         const int st = tid - 128;          // TMEM lane: token (S^T) / dimension (O^T)
@@ -673,7 +725,7 @@ pgqa_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
             const int32_t bl = find_seq(pre, p.B, p.Hkv, ce - 1);
             const int32_t nl = (int32_t)(pre[bl + 1] - pre[bl]);
             const int64_t rl = ce - 1 - (int64_t)pre[bl] * p.Hkv;
-            const int32_t jl = (int32_t)(rl / nl);
+            const int32_t jl = (rl <= kSmallProduct) ? (int32_t)((uint32_t)rl / (uint32_t)nl) : (int32_t)(rl / nl);
             const int32_t cl = (int32_t)(rl - (int64_t)jl * nl);
             last_b = bl;
             last_j = jl;
@@ -695,9 +747,13 @@ pgqa_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
             if (NP == 16) reinterpret_cast<float*>(p.rec_o)[(slot * NP + r) * kHeadDim + st] = v;
             else reinterpret_cast<__nv_bfloat16*>(p.rec_o)[(slot * NP + r) * kHeadDim + st] = __float2bfloat16_rn(v);
         };
-        // arrival on the counter of a cut unit whose record this CTA has written, and the
-        // merge of all its records by the last CTA to arrive
-        auto arrive_merge = [&](int32_t b, int32_t kvh, int32_t n, bool live, bool& arrived) -> bool {
+        // bit 0 / 1: this CTA arrived last on the slice's first / last cut unit (their
+        // records are merged after the stream); bit 2: the first one went to warp 2
+        uint32_t mg_mask = 0;
+        // arrival on the counter of a cut unit whose record this CTA has written; the last
+        // CTA to arrive queues the unit's merge
+        auto arrive_merge = [&](int32_t b, int32_t kvh, int32_t n, bool live, bool& arrived,
+                                uint32_t bit) -> bool {
             const int64_t ubeg = (int64_t)pre[b] * p.Hkv + (int64_t)kvh * n;
             const int64_t c_first = slice_owner(ubeg, nct, T);
             const int64_t c_last = slice_owner(ubeg + n - 1, nct, T);
@@ -726,7 +782,14 @@ pgqa_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
                 xword[(xg_n & 1) * 4] = last;
             }
             if (!xsync()) return false;
-            if (!xword[((xg_n - 1) & 1) * 4]) return true;
+            if (xword[((xg_n - 1) & 1) * 4]) mg_mask |= bit;  // last: merge after the stream
+            return true;
+        };
+        // merge of every CTA's record of the unit (b, kvh) of n chunks, by the last arriver
+        auto merge_records = [&](int32_t b, int32_t kvh, int32_t n) {
+            const int64_t ubeg = (int64_t)pre[b] * p.Hkv + (int64_t)kvh * n;
+            const int64_t c_first = slice_owner(ubeg, nct, T);
+            const int64_t c_last = slice_owner(ubeg + n - 1, nct, T);
             /* Merge the unit's records.  Thread st owns dims [8 dc, 8 dc + 8) of rows
              * [kR rg, kR rg + kR) (dc = st % 16, rg = st / 16), so every load is a 16-byte
              * vector; records are read kB at a time, all loads of a batch in flight
@@ -822,8 +885,8 @@ pgqa_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
                             (den[r] > 0.f ? mx[r] + ptx::lg2(den[r]) : -INFINITY) * 0.6931471805599453f;
                 }
             }
-            return true;
         };
+
 
         struct Pending {
             int pc = -1;
@@ -833,7 +896,8 @@ pgqa_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
         } pend;
         // epilogue of piece P: O^T out of TMEM, row sums and maxima from shared memory,
         // then the output rows (a whole unit) or a record and the arrival (a cut unit)
-        auto epilogue = [&](const Pending& P) -> bool {
+        // handoff: a cut first piece ending mid-stream leaves its arrival to warp 2
+        auto epilogue = [&](const Pending& P, bool handoff) -> bool {
             const int ob = P.pc & 1;
             if (!wait_all(OFULL(ob), (P.pc >> 1) & 1)) return false;
             ptx::tc_fence_after();
@@ -885,7 +949,16 @@ pgqa_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
                 for (int k = st; k < (f32 ? NP * 32 : NP * 16); k += 128) d4[k] = s4[k];
             }
             if (P.whole) return true;
-            return arrive_merge(P.b, P.kvh, P.n, true, P.is_first ? done_cut_first : done_cut_last);
+            if (handoff && P.is_first) {
+                // warp 2 takes the release and the arrival (two round trips the stream would
+                // otherwise wait for); one arrival per warp after its record stores
+                __syncwarp();
+                if (lane == 0) ptx::mbar_arrive(RECDONE);
+                mg_mask |= 4u;
+                return true;
+            }
+            return arrive_merge(P.b, P.kvh, P.n, true, P.is_first ? done_cut_first : done_cut_last,
+                                P.is_first ? 1u : 2u);
         };
 
         Tile t;
@@ -1069,19 +1142,38 @@ pgqa_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
                 nx.whole = (piece_c0 == 0) && (t.c0 + t.nc == t.n);
                 nx.is_first = cut_first && t.b == first_b && t.kvh == first_j && piece_c0 != 0;
                 // a piece still pending here had only this one tile after it
-                if (pend.pc >= 0 && !epilogue(pend)) { ok = false; break; }
+                if (pend.pc >= 0 && !epilogue(pend, true)) { ok = false; break; }
                 pend = nx;
             } else if (pend.pc >= 0 && pend.pc < pc) {
                 // one tile after a piece ended (its partials were stored before this tile's
                 // exchange, its last PV has long been issued): its epilogue runs now
-                if (!epilogue(pend)) { ok = false; break; }
+                if (!epilogue(pend, true)) { ok = false; break; }
                 pend.pc = -1;
             }
             ++i;
         }
         if (ok && pend.pc >= 0) {
             // the last piece's partials become visible to every warp at this exchange
-            ok = xsync() && epilogue(pend);
+            ok = xsync() && epilogue(pend, false);
+        }
+        if (mg_mask & 4u) {
+            // warp 2's arrival for the first cut unit (it arrives on W2DONE in every case)
+            drain_bar(W2DONE, 0);
+            __syncwarp();
+            const int32_t f = *w2flag;
+            if (f == 0) {
+                // it gave up (the call is aborting): arrive here so the counter is reset
+                arrive_merge(first_b, first_j, (int32_t)(pre[first_b + 1] - pre[first_b]), false, done_cut_first, 0u);
+            } else {
+                done_cut_first = true;
+                if (f == 2) mg_mask |= 1u;
+            }
+        }
+        // one call site for the merge code (at most two units: the slice's cut ones)
+        for (int k = 0; ok && k < 2; ++k) {
+            if (!((mg_mask >> k) & 1u)) continue;
+            const int32_t b = k == 0 ? first_b : last_b, kvh = k == 0 ? first_j : last_j;
+            merge_records(b, kvh, (int32_t)(pre[b + 1] - pre[b]));
         }
         if (!ok) {
             // a wait expired: still arrive on the counters of the units this slice cuts
@@ -1093,12 +1185,12 @@ pgqa_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
             if (cut_first && !done_cut_first) {
                 const int32_t n = (int32_t)(pre[first_b + 1] - pre[first_b]);
                 empty_record(first_b, first_j, n);
-                arrive_merge(first_b, first_j, n, false, done_cut_first);
+                arrive_merge(first_b, first_j, n, false, done_cut_first, 0u);
             }
             if (cut_last && !done_cut_last) {
                 const int32_t n = (int32_t)(pre[last_b + 1] - pre[last_b]);
                 empty_record(last_b, last_j, n);
-                arrive_merge(last_b, last_j, n, false, done_cut_last);
+                arrive_merge(last_b, last_j, n, false, done_cut_last, 0u);
             }
         }
     }

@@ -31,6 +31,7 @@ struct TcParams {
     const float* k_scale;       // e4m3 pools: dequantisation factor per KV head (null = 1)
     const float* v_scale;
     int32_t page_size, bt_stride, num_pages;
+    int32_t page_shift;         // log2(page_size) when it is a power of two, else -1
     int64_t cap_tokens;         // bt_stride * page_size
     float scale_log2;           // scale * log2(e)
     int32_t min_chunks;         // lower bound on 16-token chunks per active CTA
