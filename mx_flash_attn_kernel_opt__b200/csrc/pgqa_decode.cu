@@ -1258,12 +1258,13 @@ const Knobs& knobs() {
 // chunks per warp prefetched into L2 before griddepcontrol.wait (bf16 / e4m3 pools)
 constexpr int kDefaultSpecChunks = 4;
 constexpr int kDefaultSpecChunksKv8 = 4;
-// The pass before griddepcontrol.wait runs only when a warp streams at least this many
-// chunks: it hides behind a previous decode grid's tail, but a call with nothing ahead of
-// it pays its ~2 us in full, which only a long stream repays.  The host checks the table's
-// capacity (the pass is then left out entirely); the kernel checks the real lengths
-// before it reads the table and prefetches.
-constexpr int64_t kSpecMinChunksPerWarp = 8;
+// The pass before griddepcontrol.wait runs when a warp streams at least this many chunks
+// on average.  It hides behind a previous decode grid's tail; a call with nothing ahead
+// of it pays the pass's two round trips, less what the kept partition saves after the
+// wait (c1, isolated behind another kernel: +0.3 to +1.0 us; back to back: -1.4 us).  The
+// host checks the table's capacity (the pass is then left out entirely); the kernel
+// checks the real lengths before it reads the table and prefetches.
+constexpr int64_t kSpecMinChunksPerWarp = 1;
 
 int64_t spec_min_total_for(const pgqa_plan& plan) {
     return kSpecMinChunksPerWarp * plan.grid_ctas * plan.warps_per_cta;
