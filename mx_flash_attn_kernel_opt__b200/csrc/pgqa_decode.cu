@@ -409,42 +409,40 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
         partition();
         // the table may be far longer than the sequences: the prefetch needs real length
         if (warp < wa && T >= p.spec_min_total) {
-            {
-                const int64_t ntot = we - ws;
-                const int64_t npf = ntot < p.spec_chunks ? ntot : p.spec_chunks;
-                const int P = p.page_size;
-                int32_t b = ic0.b, n = ic0.n, j = ic0.j, c = ic0.c;
-                int32_t win_b = -1, win_p0 = 0, win_pid = 0;
-                for (int64_t k = 0; k < npf; ++k) {
-                    const int32_t page = page_of(p, c * kChunkTokens);
-                    if (b != win_b || page < win_p0 || page >= win_p0 + 32) {
-                        win_b = b;
-                        win_p0 = page;
-                        const int32_t npg = page_of(p, n * kChunkTokens + P - 1);
-                        const int32_t pg = page + lane;
-                        win_pid = (pg < npg)
-                                      ? ptx::ld_cg_s32(p.block_table + (int64_t)b * p.bt_stride + pg)
-                                      : -1;
-                        if (k == 0) { sp_b = b; sp_p0 = page; sp_npg = npg; }
+            const int64_t ntot = we - ws;
+            const int64_t npf = ntot < p.spec_chunks ? ntot : p.spec_chunks;
+            const int P = p.page_size;
+            int32_t b = ic0.b, n = ic0.n, j = ic0.j, c = ic0.c;
+            int32_t win_b = -1, win_p0 = 0, win_pid = 0;
+            for (int64_t k = 0; k < npf; ++k) {
+                const int32_t page = page_of(p, c * kChunkTokens);
+                if (b != win_b || page < win_p0 || page >= win_p0 + 32) {
+                    win_b = b;
+                    win_p0 = page;
+                    const int32_t npg = page_of(p, n * kChunkTokens + P - 1);
+                    const int32_t pg = page + lane;
+                    win_pid = (pg < npg)
+                                  ? ptx::ld_cg_s32(p.block_table + (int64_t)b * p.bt_stride + pg)
+                                  : -1;
+                    if (k == 0) { sp_b = b; sp_p0 = page; sp_npg = npg; }
+                }
+                const int32_t pid = __shfl_sync(0xffffffffu, win_pid, page - win_p0);
+                if (lane == 0 && (uint32_t)pid < (uint32_t)p.num_pages) {
+                    const int32_t kvh = (p.n_w == 1) ? j : j / p.n_w;
+                    const int32_t z = pid * P + (c * kChunkTokens - page * P);
+                    ptx::tma_prefetch_l2_3d(&kmap, 0, kvh, z);
+                    ptx::tma_prefetch_l2_3d(&vmap, 0, kvh, z);
+                    if (!KV8) {
+                        ptx::tma_prefetch_l2_3d(&kmap, 64, kvh, z);
+                        ptx::tma_prefetch_l2_3d(&vmap, 64, kvh, z);
                     }
-                    const int32_t pid = __shfl_sync(0xffffffffu, win_pid, page - win_p0);
-                    if (lane == 0 && (uint32_t)pid < (uint32_t)p.num_pages) {
-                        const int32_t kvh = (p.n_w == 1) ? j : j / p.n_w;
-                        const int32_t z = pid * P + (c * kChunkTokens - page * P);
-                        ptx::tma_prefetch_l2_3d(&kmap, 0, kvh, z);
-                        ptx::tma_prefetch_l2_3d(&vmap, 0, kvh, z);
-                        if (!KV8) {
-                            ptx::tma_prefetch_l2_3d(&kmap, 64, kvh, z);
-                            ptx::tma_prefetch_l2_3d(&vmap, 64, kvh, z);
-                        }
-                    }
-                    if (k + 1 < npf && ++c == n) {  // step to the next chunk (one exists)
-                        c = 0;
-                        if (++j == p.U) {
-                            j = 0;
-                            do { ++b; } while (pre[b + 1] == pre[b]);
-                            n = (int32_t)(pre[b + 1] - pre[b]);
-                        }
+                }
+                if (k + 1 < npf && ++c == n) {  // step to the next chunk (one exists)
+                    c = 0;
+                    if (++j == p.U) {
+                        j = 0;
+                        do { ++b; } while (pre[b + 1] == pre[b]);
+                        n = (int32_t)(pre[b + 1] - pre[b]);
                     }
                 }
             }
@@ -452,8 +450,8 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
     }
 
     // Launched as a programmatic dependent: everything above overlaps the previous
-    // kernel's tail; of what was read before this point only the checked prefix table
-    // is used after it.
+    // kernel's tail; of what was read before this point only the prefix table, once
+    // checked, and the partition computed from it are used after it.
     ptx::griddep_wait();
 
     // The warp's first window is read again now (the pass's values may be stale), in the
