@@ -22,7 +22,9 @@
  *   warp 1      MMA issuer (one thread): QK^T of tile i+1 is issued before PV of tile i, so
  *               the softmax of one tile overlaps the tensor core's work on its neighbours.
  *   warp 2      Q loader: a unit's query rows into shared memory (e4m3 pools: q split into
- *               two exact e4m3 terms, hi + lo, with a power-of-two row scale).
+ *               two exact e4m3 terms, hi + lo, with a power-of-two row scale); it also makes
+ *               the counter arrival for the slice's first piece when that piece ends
+ *               mid-stream, so the softmax warps do not wait for its round trips.
  *   warps 4-7   softmax and epilogue: thread t owns TMEM lane t, i.e. token t of S^T and
  *               dimension t of O^T.  Online softmax in the log2 domain with a lazily moved
  *               reference max (it moves only when a score exceeds it by 2^8; the O^T
