@@ -314,6 +314,7 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
     static_assert((kEarlyStash ? NG : 2) * sizeof(Stash) <= (size_t)S * kStage,
                   "the states a warp parks in its ring must fit in it");
     static_assert(W * kStates <= 32, "parked states are scanned one per lane");
+    static_assert(W <= 16, "per-warp scan words live in misc[0, 32)");
     extern __shared__ uint8_t smem_raw[];
     // 128-byte TMA swizzle needs 1024-byte aligned stages (shared-window offset).
     uint8_t* smem = smem_raw + ((1024u - (ptx::smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -344,19 +345,30 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
     const int sb0 = min(p.B, tid * per_thread);
     const int sb1 = min(p.B, sb0 + per_thread);
     auto scan_prefix = [&](auto load_len) {
-        uint32_t local = 0;
-        for (int b = sb0; b < sb1; ++b)
-            local += (uint32_t)seq_chunks((int64_t)load_len(b) + p.len_add, p.cap_tokens);
+        uint32_t local = 0, cmin = 0xffffffffu, cmax = 0;
+        for (int b = sb0; b < sb1; ++b) {
+            const uint32_t nb = (uint32_t)seq_chunks((int64_t)load_len(b) + p.len_add, p.cap_tokens);
+            local += nb;
+            cmin = min(cmin, nb);
+            cmax = max(cmax, nb);
+        }
         uint32_t incl = local;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
             const uint32_t v = __shfl_up_sync(0xffffffffu, incl, o);
             if (lane >= o) incl += v;
         }
-        if (lane == 31) misc[warp] = (int32_t)incl;
+        cmin = __reduce_min_sync(0xffffffffu, cmin);
+        cmax = __reduce_max_sync(0xffffffffu, cmax);
+        if (lane == 31) {
+            misc[warp] = (int32_t)incl;
+            // the warp's common chunk count; -1: its sequences differ; -2: it has none
+            misc[16 + warp] = cmin > cmax ? -2 : (cmin == cmax ? (int32_t)cmin : -1);
+        }
         __syncthreads();
         uint32_t run = incl - local;
         for (int w2 = 0; w2 < warp; ++w2) run += (uint32_t)misc[w2];
+
         if (tid == NT - 1) pre[p.B] = run + local;
         for (int b = sb0; b < sb1; ++b) {
             pre[b] = run;
@@ -392,6 +404,17 @@ pgqa_decode_kernel(const __grid_constant__ CUtensorMap kmap,
     auto partition = [&]() {
         T = (int64_t)pre[p.B] * p.U;
         nct = T > 0 ? active_ctas(T, gridDim.x, W, p.min_chunks) : 0;
+        if ((int64_t)p.B * p.U <= nct && nct % ((int64_t)p.B * p.U) != 0) {
+            // every warp of the scan saw the same non-zero chunk count: equal units
+            int32_t u = -2;
+            bool same = true;
+            for (int w2 = 0; w2 < W; ++w2) {
+                const int32_t v = misc[16 + w2];
+                if (v == -1 || (v >= 0 && u >= 0 && v != u)) same = false;
+                if (v >= 0) u = v;
+            }
+            nct = align_ctas(nct, (int64_t)p.B * p.U, same && u > 0);
+        }
         wa = 0;
         if ((int64_t)blockIdx.x >= nct) return;
         cs = slice_begin(blockIdx.x, nct, T);
@@ -2069,7 +2092,11 @@ extern "C" int64_t pgqa_simulate_partition(const int32_t* seq_lens, int64_t B, i
         return lo * U + (x - pre[lo] * U) / n;
     };
     const int64_t W = plan->warps_per_cta;
-    const int64_t nct = active_ctas(T, plan->grid_ctas, W, plan->min_chunks_per_warp);
+    bool uniform = true;
+    for (int64_t b = 1; b < B; ++b)
+        if (pre[b + 1] - pre[b] != pre[1] - pre[0]) uniform = false;
+    uniform = uniform && pre[1] > 0;
+    const int64_t nct = align_ctas(active_ctas(T, plan->grid_ctas, W, plan->min_chunks_per_warp), B * U, uniform);
     for (int64_t c = 0; c < nct; ++c) {
         const int64_t cs = slice_begin(c, nct, T), ce = slice_begin(c + 1, nct, T);
         for (int64_t u = unit_of(cs); u <= unit_of(ce - 1); ++u) ctas_per_unit[u] += 1;

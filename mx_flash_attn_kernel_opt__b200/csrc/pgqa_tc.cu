@@ -345,12 +345,15 @@ pgqa_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
         const int per = (p.B + kThreads - 1) / kThreads;
         const int s0 = min(p.B, tid * per), s1 = min(p.B, s0 + per);
         int32_t bad = 0;
-        uint32_t local = 0;
+        uint32_t local = 0, cmin = 0xffffffffu, cmax = 0;
         for (int b = s0; b < s1; ++b) {
             const int32_t L0 = __ldg(p.seq_lens + b);
             const int64_t Lk = (int64_t)L0 + p.len_add;
             if (L0 < 0 || Lk > p.cap_tokens) bad = 1;
-            local += (uint32_t)seq_chunks(Lk, p.cap_tokens);
+            const uint32_t nb = (uint32_t)seq_chunks(Lk, p.cap_tokens);
+            local += nb;
+            cmin = min(cmin, nb);
+            cmax = max(cmax, nb);
         }
         uint32_t incl = local;
 #pragma unroll
@@ -358,7 +361,14 @@ pgqa_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
             const uint32_t v = __shfl_up_sync(0xffffffffu, incl, o);
             if (lane >= o) incl += v;
         }
-        if (lane == 31) wsum[warp] = (int32_t)incl;
+        cmin = __reduce_min_sync(0xffffffffu, cmin);
+        cmax = __reduce_max_sync(0xffffffffu, cmax);
+        if (lane == 31) {
+            wsum[warp] = (int32_t)incl;
+            // the warp's common chunk count (-1: its sequences differ, -2: it has none), in
+            // the row-maximum buffer, which the softmax warps first use after the TMEM barrier
+            reinterpret_cast<int32_t*>(red)[warp] = cmin > cmax ? -2 : (cmin == cmax ? (int32_t)cmin : -1);
+        }
         __syncthreads();
         uint32_t run = incl - local;
         for (int w2 = 0; w2 < warp; ++w2) run += (uint32_t)wsum[w2];
@@ -382,7 +392,17 @@ pgqa_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__
     }
     const int64_t T = (int64_t)pre[p.B] * p.Hkv;
     if (T == 0) return;
-    const int64_t nct = active_ctas(T, gridDim.x, 1, p.min_chunks);
+    int64_t nct = active_ctas(T, gridDim.x, 1, p.min_chunks);
+    if ((int64_t)p.B * p.Hkv <= nct && nct % ((int64_t)p.B * p.Hkv) != 0) {  // equal units: align
+        int32_t u = -2;
+        bool same = true;
+        for (int w2 = 0; w2 < kThreads / 32; ++w2) {
+            const int32_t v = reinterpret_cast<const int32_t*>(red)[w2];
+            if (v == -1 || (v >= 0 && u >= 0 && v != u)) same = false;
+            if (v >= 0) u = v;
+        }
+        nct = align_ctas(nct, (int64_t)p.B * p.Hkv, same && u > 0);
+    }
     if ((int64_t)blockIdx.x >= nct) return;
     const int64_t cs = slice_begin(blockIdx.x, nct, T);
     const int64_t ce = slice_begin(blockIdx.x + 1, nct, T);

@@ -39,6 +39,12 @@ def py_model(seq_lens, U, cap, grid, W, minc):
     if T == 0:
         return 0, [0] * len(units), [0] * len(units), []
     nct = max(1, min(grid, T // (W * minc)))
+    # equal units: a multiple of the unit count, if that idles at most 1/32 of the CTAs
+    n_units = len(n_b) * U
+    if len(set(n_b)) == 1 and n_b[0] > 0 and nct >= n_units:
+        aligned = nct // n_units * n_units
+        if (nct - aligned) * 32 <= nct:
+            nct = aligned
     cta_sl = [(c * T // nct, (c + 1) * T // nct) for c in range(nct)]
     warp_sl = []
     for cs, ce in cta_sl:
@@ -97,10 +103,11 @@ def test_long_context_split_count_follows_sm_count():
     seq, cap = inputs.config_seq_lens("c2")
     _, plan = make_plan(2, 64, 8, 128, 16)
     n, ctas, segs = simulate(seq.tolist(), plan.units_per_seq, cap, plan)
-    assert n == 148
-    assert set(ctas.tolist()) <= {9, 10, 11}
+    # 16 equal units on 148 SMs: 144 CTAs, every unit on exactly 9 of them
+    assert n == 144
+    assert set(ctas.tolist()) == {9}
     # every warp slice adds one piece, plus one per unit boundary crossed inside a slice
-    assert 148 * plan.warps_per_cta <= segs.sum() <= 148 * plan.warps_per_cta + len(segs)
+    assert 144 * plan.warps_per_cta <= segs.sum() <= 144 * plan.warps_per_cta + len(segs)
     # with 4 SMs the same work is split 1-2 ways per unit
     st, small = make_plan(2, 64, 8, 128, 16, num_sms=4, smem_optin=232448)
     n4, ctas4, _ = simulate(seq.tolist(), small.units_per_seq, cap, small)
@@ -118,3 +125,18 @@ def test_seq_lens_clamped_to_capacity():
     n, _, segs_a = simulate([10**6, 5], plan.units_per_seq, 64, plan)
     n2, _, segs_b = simulate([64, 5], plan.units_per_seq, 64, plan)
     assert segs_a.tolist() == segs_b.tolist()
+
+
+def test_equal_units_align_with_cta_slices_only_when_cheap():
+    """Equal lengths: CTAs become a multiple of the unit count when that idles at most
+    1/32 of them (c1: 32 units -> 128 CTAs, 4 per unit); 80 units would idle 68 of 148,
+    so that call keeps 148; ragged lengths are never aligned."""
+    _, plan = make_plan(4, 32, 8, 128, 16)
+    n, ctas, _ = simulate([1024] * 4, plan.units_per_seq, 1024, plan)
+    assert n == 128 and set(ctas.tolist()) == {4}
+    _, plan = make_plan(10, 80, 8, 128, 16)
+    n, _, _ = simulate([32768] * 10, plan.units_per_seq, 32768, plan)
+    assert n == 148
+    _, plan = make_plan(2, 64, 8, 128, 16)
+    n, _, _ = simulate([32768, 32752], plan.units_per_seq, 32768, plan)
+    assert n == 148
